@@ -1,0 +1,407 @@
+"""Benchmark: batched Dirichlet-Thompson search step on B200.
+
+Workload (isolated search kernels): Hex 9x9 action space (82 actions), 4096
+lanes per GPU, 128 simulations, tree capacity 129, synthetic network outputs
+(scacchi_b200/synthetic.py), guarded prefix-CDF estimator (kappa 1, Q21,
+Monte Carlo fallback with 8 samples), root policy with 8 samples and the
+search-evidence Q21 root readout.  One step = one ``search(root_state, key)``
+call through the public boundary (root evaluation, 128 simulations, root
+policy, readout, target packing).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+Under torchrun (N > 1) every rank searches its own 4096 lanes (weak scaling)
+and the root targets are all-gathered over NCCL at the end of the step.
+Prints one JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Hex 9×9 search sims/sec (lanes×sims) at 1/2/4/8 B200; leaf evals/sec"
+LANES = 4096
+SIMS = 128
+ACTIONS = 82
+FALLBACK_SAMPLES = 8
+ROOT_SAMPLES = 8
+KAPPA = 1.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def workload_config(world: int) -> dict:
+    return {
+        "workload": "isolated search kernels: Hex 9x9 (82 actions), synthetic network outputs",
+        "lanes_per_gpu": LANES, "global_lanes": LANES * world, "num_simulations": SIMS,
+        "tree_capacity": SIMS + 1, "num_actions": ACTIONS, "estimator": "prefix_cdf Q21 + MC fallback",
+        "kappa": KAPPA, "fallback_policy_samples": FALLBACK_SAMPLES, "root_policy_samples": ROOT_SAMPLES,
+        "degenerate_lanes": "1% (alpha=1e-3)", "legal_prob": 0.7, "logc": "clip(N(0.5,1),-4,6)",
+        "l2": "inputs larger than L2: the tree is 0.9 GB per GPU, rewritten every step",
+        "parallelism": f"dp{world} (lane-sharded)",
+    }
+
+
+def read_peaks() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(float(r[1]) for r in rows), "sm_max_mhz": float(rows[0][2]),
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def search_config():
+    from scacchi_b200.types import (DirichletThompsonSearchConfig, NumericalPosteriorUpdateConfig,
+                                    PosteriorUpdateConfig, PosteriorUpdateKind, RootPolicySupport)
+
+    return DirichletThompsonSearchConfig(
+        num_simulations=SIMS, max_depth=SIMS, root_policy_support=RootPolicySupport.search_evidence,
+        policy_target_temperature=1.0,
+        posterior_update=PosteriorUpdateConfig(
+            kind=PosteriorUpdateKind.numerical,
+            numerical=NumericalPosteriorUpdateConfig(kappa=KAPPA, half_width=10, tail_scale=8.0, min_half_range=6.0,
+                                                     max_half_range=11.0, fallback_policy_samples=FALLBACK_SAMPLES,
+                                                     fallback_policy_sample_chunk_size=32)))
+
+
+def instrumented_step(game, state, key, cfg):
+    """One extra (untimed) step driven phase by phase from Python, with CUDA
+    events on the launching stream around every kernel and the kernels' own
+    work counters, for the per-kernel roofline."""
+    import torch
+
+    from scacchi_b200 import random as R
+    from scacchi_b200.dirichlet_mctx import search as S
+    from scacchi_b200.dirichlet_mctx.tree import _init_tree
+    from scacchi_b200.play_search import _make_posterior_update
+    from scacchi_b200.dirichlet_mctx.posterior_updates import rule_params
+
+    dev = state.observation.device
+    pred = game.evaluator(state.observation)
+    from scacchi_b200.dirichlet_mctx import RootFnOutput
+
+    root = RootFnOutput(prior_logits=pred.logits, value=pred.alpha_v, action_values=pred.alpha_q,
+                        embedding=state.observation,
+                        terminal_outcome=torch.full((LANES,), -1, dtype=torch.int8, device=dev),
+                        to_play=state.current_player)
+    rparams = rule_params(_make_posterior_update(cfg.posterior_update.active()))
+    search_key = R.split(key)[0]
+    tree = _init_tree(root, SIMS, ~state.legal_action_mask, full=False)
+    sched = torch.from_numpy(R.key_schedule(search_key, SIMS).view("int32")).to(dev)
+    bufs = S.SimulationBuffers(LANES, ACTIONS, tree.E, dev)
+    sim_stats = torch.zeros(2, dtype=torch.int64, device=dev)
+    bwd_stats = torch.zeros(3, dtype=torch.int64, device=dev)
+    names = ("simulate", "recurrent", "expand", "backward")
+    ev = {n: [] for n in names}
+    stream = torch.cuda.current_stream()
+    for i in range(SIMS):
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        marks[0].record(stream)
+        S.simulate(tree, sched[i, 1], SIMS, bufs, sim_stats)
+        marks[1].record(stream)
+        step, child = game((), None, bufs.action, bufs.parent_embedding[:, :tree.E])
+        marks[2].record(stream)
+        v, tp = S.expand(tree, i + 1, bufs, step, child)
+        marks[3].record(stream)
+        S.backward(tree, sched[i, 3], bufs, v, tp, rparams, bwd_stats)
+        marks[4].record(stream)
+        for j, n in enumerate(names):
+            ev[n].append((marks[j], marks[j + 1]))
+    torch.cuda.synchronize()
+    ms = {n: sum(a.elapsed_time(b) for a, b in ev[n]) for n in names}
+    return ms, sim_stats.cpu().tolist(), bwd_stats.cpu().tolist()
+
+
+def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dict:
+    A = ACTIONS
+    row = A * (4 + 4 + 8 + 1 + 1)  # children, payload, alpha, outcome, invalid
+    bwd_bytes = bwd_stats[0] * (row + 24 + A * 12 + 12) + bwd_stats[1] * 25
+    sim_bytes = sim_stats[0] * (row + 5) + sim_stats[1] * 12
+    total = sum(ms.values())
+    dominant = max(ms, key=ms.get)
+    per = {"backward": bwd_bytes, "simulate": sim_bytes}
+    bytes_per_launch = per.get(dominant, 0) / SIMS
+    avg_s = ms[dominant] / SIMS / 1e3
+    achieved = bytes_per_launch / avg_s / 1e9 if avg_s > 0 else 0.0
+    return {
+        "bound": "hbm", "kernel": f"{dominant}_kernel", "achieved": round(achieved, 2), "peak": peak,
+        "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
+        "peak_source": peak_kind,
+        "algorithmic_bytes_per_launch": int(bytes_per_launch), "avg_launch_ms": round(ms[dominant] / SIMS, 5),
+        "kernel_share": {k: round(v / total, 4) for k, v in ms.items()},
+        "work": {"descent_nodes": sim_stats[0], "descent_prior_gathers": sim_stats[1],
+                 "backward_nodes": bwd_stats[0], "backward_child_gathers": bwd_stats[1],
+                 "mc_fallback_nodes": bwd_stats[2]},
+        "note": "search kernels are ALU-bound (in-kernel threefry, Q21 transcendentals); the HBM fraction is "
+                "algorithmic bytes over measured copy bandwidth",
+    }
+
+
+def cpu_baseline(lanes: int = 48) -> dict:
+    """The C oracle (a restatement of the reference's JAX path, which cannot
+    be installed here) on a bounded sample: lanes [0, lanes) of the same
+    4096-lane workload, one host thread."""
+    from oracle import oracle as O
+
+    env = O.synth_params(seed=0)
+    rule = O.Rule(prefix_cdf=True, kappa=KAPPA, samples=FALLBACK_SAMPLES)
+    t0 = time.perf_counter()
+    O.search_synthetic(env, LANES, O.PRNGKey(0), SIMS, rule, max_depth=SIMS, policy_samples=ROOT_SAMPLES,
+                       lanes=(0, lanes))
+    dt = time.perf_counter() - t0
+    return {"value": round(lanes * SIMS / dt, 2), "unit": "sims/s", "cores": 1, "kind": "port",
+            "sample": f"lanes 0..{lanes - 1} of the {LANES}-lane x {SIMS}-simulation workload ({dt:.1f} s)"}
+
+
+def _oracle_lane_range(args):
+    lo, hi = args
+    from oracle import oracle as O
+
+    env = O.synth_params(seed=0)
+    rule = O.Rule(prefix_cdf=True, kappa=KAPPA, samples=FALLBACK_SAMPLES)
+    O.search_synthetic(env, LANES, O.PRNGKey(0), SIMS, rule, max_depth=SIMS, policy_samples=ROOT_SAMPLES,
+                       lanes=(lo, hi))
+    return hi - lo
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    """--impl reference: the reference's algorithm on the host cores (the C
+    oracle restatement; the JAX reference cannot be installed here), all
+    host threads, each step a bounded lane sample of the same workload."""
+    if rank != 0:
+        return
+    import multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    lanes_per_worker = 2
+    chunks = [(i * lanes_per_worker, (i + 1) * lanes_per_worker) for i in range(cores)]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        for _ in range(args.warmup):
+            pool.map(_oracle_lane_range, chunks[:1])
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            done = sum(pool.map(_oracle_lane_range, chunks))
+            times.append(time.perf_counter() - t0)
+    dt = sum(times) / len(times)
+    value = done * SIMS / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "sims/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(1),
+        "cpu_baseline": {"value": round(value, 2), "unit": "sims/s", "cores": cores, "kind": "port",
+                         "sample": f"{done} lanes of the {LANES}-lane workload per step, {cores} processes"},
+        "e2e": {"value": round(value, 2), "unit": "sims/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference is pure JAX (jax/flax/pgx not installable offline); timed: the C oracle restatement",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+
+    from scacchi_b200 import _lib
+    from scacchi_b200 import random as R
+    from scacchi_b200.play_search import make_search
+    from scacchi_b200.synthetic import SyntheticGame, SyntheticGameConfig
+
+    game = SyntheticGame(SyntheticGameConfig(seed=rank, num_actions=ACTIONS), device=dev)
+    cfg = search_config()
+    search = make_search(game, game.evaluator, cfg)
+    key = R.split(R.PRNGKey(0), world)[rank]  # play.py:231,243: per-device keys
+    state = game.init(LANES)
+    torch.cuda.synchronize()
+
+    def gather(targets):
+        if world > 1:
+            pol = targets.prediction.policy.contiguous()
+            out = torch.empty((world * LANES, ACTIONS), dtype=pol.dtype, device=dev)
+            dist.all_gather_into_tensor(out, pol)
+            act = targets.metadata.search_action.contiguous()
+            acts = torch.empty((world * LANES,), dtype=act.dtype, device=dev)
+            dist.all_gather_into_tensor(acts, act)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing -------------------------------------------
+    for _ in range(args.warmup):
+        gather(search(state, key))
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count()
+    stream = torch.cuda.current_stream()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            gather(search(state, key))
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - launches0
+    ms_step = max_over_ranks(start.elapsed_time(stop) / args.steps)
+    value = world * LANES * SIMS / (ms_step / 1e3)
+    evals = world * LANES * (SIMS + 1) / (ms_step / 1e3)
+
+    # ---- end to end: host buffers through the public call ------------------
+    host_obs = state.observation.cpu().pin_memory()
+    host_legal = state.legal_action_mask.cpu().pin_memory()
+    host_player = state.current_player.cpu().pin_memory()
+    out_policy = torch.empty((LANES, ACTIONS), dtype=torch.float32).pin_memory()
+    out_alpha_q = torch.empty((LANES, ACTIONS, 2), dtype=torch.float32).pin_memory()
+    out_alpha_v = torch.empty((LANES, 2), dtype=torch.float32).pin_memory()
+    out_action = torch.empty((LANES,), dtype=torch.int32).pin_memory()
+    h2d = host_obs.numel() + host_legal.numel() + host_player.numel() * 4
+    d2h = (out_policy.numel() + out_alpha_q.numel() + out_alpha_v.numel() + out_action.numel()) * 4
+
+    def e2e_step():
+        from scacchi_b200.synthetic import SyntheticState
+
+        s = SyntheticState(observation=host_obs.to(dev, non_blocking=True),
+                           legal_action_mask=host_legal.to(dev, non_blocking=True),
+                           current_player=host_player.to(dev, non_blocking=True),
+                           rewards=torch.zeros((LANES, 2), device=dev),
+                           terminated=torch.zeros((LANES,), dtype=torch.bool, device=dev))
+        t = search(s, key)
+        gather(t)
+        out_policy.copy_(t.prediction.policy, non_blocking=True)
+        out_alpha_q.copy_(t.prediction.alpha_q, non_blocking=True)
+        out_alpha_v.copy_(t.prediction.alpha_v, non_blocking=True)
+        out_action.copy_(t.metadata.search_action, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_value = world * LANES * SIMS / (e2e_ms / 1e3)
+
+    # ---- per-kernel roofline (one instrumented, untimed step) --------------
+    peak, peak_kind = read_peaks()
+    ms, sim_stats, bwd_stats = instrumented_step(game, state, key, cfg)
+    roof = roofline(ms, sim_stats, bwd_stats, peak, peak_kind)
+    barrier()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "sims/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(world),
+            "leaf_evals_per_s": round(evals, 2), "clocks": clocks.summary(),
+            "e2e": {"value": round(e2e_value, 2), "unit": "sims/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": int(launches), "roofline": roof,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,268 @@
+/*
+ * scacchi_b200 — C ABI of the B200 Dirichlet-Thompson search step.
+ *
+ * Every entry point takes device pointers, plain sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and returns an
+ * int status: 0 = ok, SCACCHI_EINVAL = rejected arguments (nothing was
+ * launched), SCACCHI_ECUDA = a CUDA launch error.  Device-side index checks
+ * (a tree index outside [0, num_nodes)) skip the access and raise a sticky
+ * flag read by scacchi_device_error().
+ *
+ * The reference (Francesco215/Scacchi) is pure Python/JAX; each entry point
+ * below names the function of `scacchi/dirichlet_mctx` (or of
+ * `scacchi/play_search.py`) whose semantics it implements and that a jax.ffi
+ * custom call would bind to.  Outcomes are binary (loss 0, win 1): the Hex
+ * configuration.  Actions per node: 1 <= num_actions <= 128.
+ *
+ * Tree layout (struct of arrays, lanes outermost, C = num_nodes,
+ * S = action_stride = num_actions rounded up to a multiple of 32):
+ *   parents, node_to_play, node_payload   int32   [B, C]
+ *   node_outcome                          int8    [B, C]
+ *   node_value_prior, node_value_alpha    float32 [B, C, 2]
+ *   children_index, edge_payload          int32   [B, C, S]
+ *   edge_outcome                          int8    [B, C, S]
+ *   invalid                               uint8   [B, C, S]
+ *   edge_alpha                            float32 [B, C, S, 2]
+ *   embedding                             uint8   [B, C, emb_bytes]
+ * Per-lane inputs and outputs use dense [B, A] rows.
+ *
+ * Keys are jax.random threefry key pairs (uint32[2]) in device memory.
+ */
+#ifndef SCACCHI_B200_H
+#define SCACCHI_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SCACCHI_OK 0
+#define SCACCHI_EINVAL 1
+#define SCACCHI_ECUDA 2
+
+typedef struct {
+  int32_t batch;
+  int32_t num_nodes;
+  int32_t num_actions;
+  int32_t action_stride;
+  int32_t emb_bytes;
+  int32_t *parents;
+  int32_t *children_index;
+  int32_t *node_to_play;
+  int8_t *node_outcome;
+  int32_t *node_payload;
+  int8_t *edge_outcome;
+  int32_t *edge_payload;
+  float *node_value_prior;
+  float *node_value_alpha;
+  float *edge_alpha;
+  uint8_t *invalid;
+  uint8_t *embedding;
+} scacchi_tree;
+
+/* Static parameters of the two built-in posterior repair rules
+ * (posterior_updates.py:220-367). */
+typedef struct {
+  int32_t rule;              /* 0: update_posterior (Monte Carlo), 1: update_posterior_prefix_cdf */
+  int32_t kappa_ge_one;      /* kappa >= 1, decided in double precision */
+  float inv_kappa;           /* float32(1 / kappa) */
+  float kappa;               /* float32(kappa) */
+  int32_t samples;           /* policy_samples (rule 0) / fallback_policy_samples (rule 1) */
+  int32_t half_width;        /* Q = 2 * half_width + 1 grid points */
+  float tail_scale;
+  float min_half_range;
+  float max_half_range;
+  float density_tol;         /* density_log_integral_tolerance */
+} scacchi_update_params;
+
+/* Prefix-CDF estimator outputs (BinaryPrefixQuadraturePolicy, prefix_cdf.py:21-37). */
+typedef struct {
+  float *policy;                   /* [B, A] */
+  float *raw_policy;               /* [B, A] */
+  float *raw_mass;                 /* [B] */
+  float *normalization_error;      /* [B] */
+  uint8_t *finite;                 /* [B] */
+  float *grid_half_range;          /* [B] */
+  uint8_t *tail_range_clipped;     /* [B] */
+  float *density_log_integral;     /* [B, A] */
+  int32_t *fallback_interval_count;/* [B] */
+} scacchi_prefix_out;
+
+/* Synthetic-game parameters (isolated search-kernel workload). */
+typedef struct {
+  uint32_t seed_k0, seed_k1;
+  int32_t num_actions;
+  float legal_prob;
+  float terminal_prob;
+  float degenerate_lane_prob;
+  float degenerate_alpha;
+  float logc_mean, logc_std, logc_min, logc_max;
+} scacchi_synthetic_params;
+
+/* ---- search core (scacchi/dirichlet_mctx) ---------------------------- */
+
+/* instantiate_tree_from_root (tree.py:245-277).  full_init != 0 writes the
+ * defaults of every node slot; full_init == 0 writes only the root row and
+ * leaves slots 1..C-1 to scacchi_expand(lazy_init=1), which writes each slot
+ * exactly once, before any read.  root_embedding may be NULL. */
+int scacchi_tree_init(const scacchi_tree *tree, const float *root_value, const float *root_action_values,
+                      const uint8_t *root_invalid, const int8_t *root_terminal, const int32_t *root_to_play,
+                      const uint8_t *root_embedding, int32_t full_init, void *stream);
+
+/* simulate / _simulate_one (search.py:21-78): one warp per lane walks the
+ * tree with Thompson selection until an unvisited edge, a categorical or
+ * unsearchable child, or max_depth.  simulate_key: uint32[2].  When
+ * parent_embedding is non-NULL the selected parent's embedding row is
+ * gathered into it ([B, emb_bytes]).  stats (may be NULL) accumulates
+ * uint64[2]: nodes selected from, child value priors gathered. */
+int scacchi_simulate(const scacchi_tree *tree, const uint32_t *simulate_key, int32_t max_depth,
+                     int32_t *parent, int32_t *action, uint8_t *active, uint8_t *parent_embedding,
+                     uint64_t *stats, void *stream);
+
+/* expand (search.py:101-143).  step_* are the recurrent_fn outputs
+ * (RecurrentFnOutput, base.py:58-74); child_embedding may be NULL.
+ * lazy_init != 0 also writes the defaults of slot new_node for lanes that do
+ * not initialise it (see scacchi_tree_init). */
+int scacchi_expand(const scacchi_tree *tree, int32_t new_node, const int32_t *parent, const int32_t *action,
+                   const uint8_t *active, const float *step_value, const float *step_action_values,
+                   const uint8_t *step_invalid, const int8_t *step_terminal, const int32_t *step_to_play,
+                   const uint8_t *child_embedding, int32_t lazy_init, void *stream);
+
+/* backward (search.py:146-171) with the posterior update rule of `params`
+ * (update_posterior / update_posterior_prefix_cdf, posterior_updates.py)
+ * and _categorize_node_and_publish (utils.py:67-124).  stats (may be NULL)
+ * accumulates uint64[3]: node updates, visited children gathered,
+ * prefix-CDF updates that fell back to Monte Carlo. */
+int scacchi_backward(const scacchi_tree *tree, const uint32_t *backward_key, const int32_t *parent,
+                     const int32_t *action, const uint8_t *active, const float *step_value,
+                     const int32_t *step_to_play, const scacchi_update_params *params,
+                     uint64_t *stats, void *stream);
+
+/* dirichlet_thompson_policy root readout (policies.py:28-42): one-hot on the
+ * sampled certified action of a categorical root, else posterior_best_policy
+ * with max(1, policy_samples) draws; then masked_argmax. */
+int scacchi_root_policy(const scacchi_tree *tree, const uint32_t *policy_key, const uint8_t *invalid,
+                        int32_t policy_samples, float *action_weights, int32_t *action, void *stream);
+
+/* Tree.summary (tree.py:212-242). */
+int scacchi_summary(const scacchi_tree *tree, float *visit_counts, float *alpha, float *value_alpha,
+                    int8_t *q_outcome, int32_t *q_distance, int8_t *v_outcome, int32_t *v_distance,
+                    void *stream);
+
+/* ---- estimators ------------------------------------------------------- */
+
+/* binary_posterior_best_policy_prefix_quadrature (prefix_cdf.py:217-445)
+ * on alpha [B, A, 2]; categorical_outcome may be NULL (all unresolved). */
+int scacchi_prefix_cdf(const float *alpha, const uint8_t *invalid, const int8_t *categorical_outcome,
+                       int32_t batch, int32_t num_actions, int32_t half_width, float tail_scale,
+                       float min_half_range, float max_half_range, const scacchi_prefix_out *out,
+                       void *stream);
+
+/* posterior_best_policy (action_selection.py:146-194) on alpha [B, A, 2];
+ * categorical_outcome may be NULL. */
+int scacchi_posterior_best_policy(const uint32_t *key, const float *alpha, const uint8_t *invalid,
+                                  const int8_t *categorical_outcome, int32_t batch, int32_t num_actions,
+                                  int32_t num_samples, float *policy, void *stream);
+
+/* thompson_sample (action_selection.py:135-143) on alpha [B, A, 2]. */
+int scacchi_thompson_sample(const uint32_t *key, const float *alpha, const uint8_t *invalid,
+                            const int8_t *categorical_outcome, int32_t batch, int32_t num_actions,
+                            int32_t *action, void *stream);
+
+/* update_posterior / update_posterior_prefix_cdf on explicit contexts
+ * (PosteriorUpdateContext, tree.py:30-83), struct-of-arrays with a leading
+ * batch axis; the field order is that of scacchi_context below. */
+typedef struct {
+  const uint8_t *active;
+  const uint8_t *leaf_active;
+  const int32_t *leaf_action;
+  const float *leaf_value;
+  const int32_t *leaf_to_play;
+  const int32_t *node_to_play;
+  const int32_t *node_payload;
+  const float *value_prior;
+  const float *value_alpha;
+  const float *edge_alpha;
+  const int32_t *edge_payload;
+  const int8_t *edge_outcome;
+  const uint8_t *invalid;
+  const uint8_t *child_visited;
+  const float *child_prior;
+  const float *child_value;
+  const int32_t *child_payload;
+  const int8_t *child_outcome;
+  const int32_t *child_to_play;
+} scacchi_context;
+
+int scacchi_update_posterior(const uint32_t *key, const scacchi_context *context, int32_t batch,
+                             int32_t num_actions, const scacchi_update_params *params, float *edge_alpha,
+                             int32_t *edge_payload, float *value_alpha, uint8_t *unsafe, void *stream);
+
+/* ---- search boundary (scacchi/play_search.py) ------------------------- */
+
+/* _dirichlet_root_policy_readout with the numerical update
+ * (play_search.py:161-364): search-evidence support, Q21 readout with the
+ * native fallback, categorical population, power-temperature
+ * renormalisation.  All inputs are the root summary ([B, A] / [B]). */
+int scacchi_root_readout(int32_t batch, int32_t num_actions, const float *native_policy,
+                         const float *visit_counts, const float *alpha, const int8_t *q_outcome,
+                         const int32_t *q_distance, const int8_t *v_outcome, const uint8_t *legal,
+                         int32_t search_evidence_support, float temperature, int32_t half_width,
+                         float tail_scale, float min_half_range, float max_half_range, float *policy_target,
+                         uint8_t *accepted, void *stream);
+
+/* ---- synthetic game (isolated search-kernel workload) ----------------- */
+
+int scacchi_synthetic_root(const scacchi_synthetic_params *params, int32_t batch, float *prior_logits,
+                           float *value, float *action_values, uint8_t *invalid, int8_t *terminal,
+                           int32_t *to_play, uint8_t *embedding, void *stream);
+
+/* Network outputs of given states ([B, 16] bytes), no step. */
+int scacchi_synthetic_evaluate(const scacchi_synthetic_params *params, int32_t batch, const uint8_t *states,
+                               float *prior_logits, float *value, float *action_values, uint8_t *invalid,
+                               int8_t *terminal, int32_t *to_play, void *stream);
+
+int scacchi_synthetic_recurrent(const scacchi_synthetic_params *params, int32_t batch, const int32_t *action,
+                                const uint8_t *parent_embedding, float *value, float *action_values,
+                                uint8_t *invalid, int8_t *terminal, int32_t *to_play, uint8_t *child_embedding,
+                                void *stream);
+
+/* The whole simulation loop on the synthetic game (search.py:189-251):
+ * for i < num_simulations: simulate, recurrent, expand(lazy), backward.
+ * `keys` holds the per-simulation key schedule uint32[num_simulations, 4, 2]
+ * (split(key, 4) chain), `workspace` at least scacchi_search_workspace_bytes()
+ * bytes of device memory.  The tree root must already be initialised. */
+size_t scacchi_search_workspace_bytes(int32_t batch, int32_t num_actions, int32_t emb_bytes);
+/* stats (may be NULL): uint64[6] = backward stats [0..2], unused [3],
+ * simulate stats [4..5]. */
+int scacchi_search_synthetic(const scacchi_tree *tree, const scacchi_synthetic_params *env,
+                             const uint32_t *keys, int32_t num_simulations, int32_t max_depth,
+                             const scacchi_update_params *params, void *workspace, uint64_t *stats,
+                             void *stream);
+
+/* ---- host-side jax.random key helpers (no device work) ---------------- */
+
+/* search.py:207-209 key chain: for i < num_simulations,
+ * (key_{i+1}, simulate, expand, backward) = split(key_i, 4); key_0 is the
+ * search key.  out: uint32[num_simulations, 4, 2]. */
+int scacchi_key_schedule(uint32_t k0, uint32_t k1, int32_t num_simulations, uint32_t *out);
+/* jax.random.split(key, n) -> out uint32[n, 2] */
+int scacchi_split_host(uint32_t k0, uint32_t k1, int32_t n, uint32_t *out);
+/* jax.random.fold_in(key, data) -> out uint32[2] */
+int scacchi_fold_in_host(uint32_t k0, uint32_t k1, uint32_t data, uint32_t *out);
+
+/* ---- diagnostics ------------------------------------------------------- */
+
+/* Sticky device-side error flags (bit 0: tree index out of range); reading
+ * synchronises the device and clears the flags. */
+int scacchi_device_error(uint32_t *flags);
+
+/* Number of kernels this library has launched since load (all streams). */
+uint64_t scacchi_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCACCHI_B200_H */

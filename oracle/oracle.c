@@ -453,7 +453,15 @@ typedef struct {
   float *edge_alpha;
   uint8_t *invalid;
   uint8_t *embedding;
+  /* The tree may hold lanes [lane_offset, lane_offset + B) of a batch of
+   * total_batch lanes (0 = B): lane-indexed random streams use the global
+   * lane index and batch size, so any lane range reproduces the full run. */
+  int lane_offset;
+  int total_batch;
 } or_tree;
+
+static int glane(const or_tree *t, int b) { return b + t->lane_offset; }
+static int gbatch(const or_tree *t) { return t->total_batch > 0 ? t->total_batch : t->B; }
 
 typedef struct {
   int rule;               /* 0: update_posterior (MC), 1: update_posterior_prefix_cdf */
@@ -535,7 +543,7 @@ void or_simulate(const or_tree *t, sk_key simulate_key, int max_depth, int32_t *
   float alpha[2 * MAX_ACTIONS];
   uint8_t masked[MAX_ACTIONS];
   for (int b = 0; b < t->B; ++b) {
-    sk_key key = sk_split(simulate_key, (uint64_t)b);
+    sk_key key = sk_split(simulate_key, (uint64_t)glane(t, b));
     int root_active = t->node_outcome[NODE(t, b, 0)] == NO_OUTCOME && any_searchable(t, b, 0);
     int node = 0, next = 0, action = 0, depth = 0, cont = root_active;
     while (cont) {
@@ -867,7 +875,7 @@ long or_backward(or_tree *t, sk_key backward_key, const int32_t *sim_parent, con
     while (active) {
       sk_key next_key = sk_split(key, 0), update_key = sk_split(key, 1);
       gather_context(t, b, node, active, leaf_active, sim_action[b], step_value + 2 * b, step_to_play[b], ctx);
-      posterior_update_lane(update_key, ctx, t->A, u, b, t->B, upd);
+      posterior_update_lane(update_key, ctx, t->A, u, glane(t, b), gbatch(t), upd);
       unsafe_count += upd->unsafe;
       set_node_update(t, b, node, upd);
       categorize_and_publish(t, b, node);
@@ -923,7 +931,7 @@ void or_root_policy(const or_tree *t, sk_key policy_key, const uint8_t *invalid,
       int count = categorical_candidates(t->node_outcome[ri], t->edge_outcome + EDGE(t, b, 0, 0),
                                          t->edge_payload + EDGE(t, b, 0, 0), inv, A, tied);
       for (int a = 0; a < A; ++a) {
-        float u = sk_uniform_tiny(tie_key, (uint64_t)b * A + a);
+        float u = sk_uniform_tiny(tie_key, (uint64_t)glane(t, b) * A + a);
         float g = -sm_logf(-sm_logf(u));
         noise[a] = g + (tied[a] ? 0.0f : -SM_INF);
       }
@@ -931,8 +939,8 @@ void or_root_policy(const or_tree *t, sk_key policy_key, const uint8_t *invalid,
       for (int a = 0; a < A; ++a) w[a] = a == chosen ? 1.0f : 0.0f;
     } else {
       effective_alpha_node(t, b, 0, alpha);
-      posterior_best_policy_lane(policy_key, alpha, inv, t->edge_outcome + EDGE(t, b, 0, 0), A, S, b,
-                                 t->B, w);
+      posterior_best_policy_lane(policy_key, alpha, inv, t->edge_outcome + EDGE(t, b, 0, 0), A, S, glane(t, b),
+                                 gbatch(t), w);
     }
     float masked[MAX_ACTIONS];
     for (int a = 0; a < A; ++a) masked[a] = inv[a] ? -SM_INF : w[a];
@@ -1145,13 +1153,14 @@ static void synthetic_eval(const se_params *p, se_state s, int lane, float *valu
 }
 
 /* root network outputs + states for B lanes */
-void or_synthetic_root(const se_params *p, int B, float *logits, float *value, float *action_values,
-                       uint8_t *invalid, int8_t *terminal, int32_t *to_play, uint8_t *embedding) {
+void or_synthetic_root(const se_params *p, int B, int lane_offset, float *logits, float *value,
+                       float *action_values, uint8_t *invalid, int8_t *terminal, int32_t *to_play,
+                       uint8_t *embedding) {
   const int A = p->num_actions;
   for (int b = 0; b < B; ++b) {
-    se_state s = se_root_state(p, b);
-    synthetic_eval(p, s, b, value + 2 * b, action_values + (size_t)b * A * 2, invalid + (size_t)b * A,
-                   logits + (size_t)b * A);
+    se_state s = se_root_state(p, b + lane_offset);
+    synthetic_eval(p, s, b + lane_offset, value + 2 * b, action_values + (size_t)b * A * 2,
+                   invalid + (size_t)b * A, logits + (size_t)b * A);
     terminal[b] = (int8_t)se_terminal(p, s);
     to_play[b] = s.to_play;
     memcpy(embedding + (size_t)b * sizeof(se_state), &s, sizeof(se_state));
@@ -1159,15 +1168,16 @@ void or_synthetic_root(const se_params *p, int B, float *logits, float *value, f
 }
 
 /* recurrent_fn of the synthetic game: (parent embedding, action) -> step */
-void or_synthetic_recurrent(const se_params *p, int B, const int32_t *action, const uint8_t *parent_embedding,
-                            float *value, float *action_values, uint8_t *invalid, int8_t *terminal,
-                            int32_t *to_play, uint8_t *child_embedding) {
+void or_synthetic_recurrent(const se_params *p, int B, int lane_offset, const int32_t *action,
+                            const uint8_t *parent_embedding, float *value, float *action_values, uint8_t *invalid,
+                            int8_t *terminal, int32_t *to_play, uint8_t *child_embedding) {
   const int A = p->num_actions;
   for (int b = 0; b < B; ++b) {
     se_state ps;
     memcpy(&ps, parent_embedding + (size_t)b * sizeof(se_state), sizeof(se_state));
     se_state s = se_child_state(ps, action[b]);
-    synthetic_eval(p, s, b, value + 2 * b, action_values + (size_t)b * A * 2, invalid + (size_t)b * A, NULL);
+    synthetic_eval(p, s, b + lane_offset, value + 2 * b, action_values + (size_t)b * A * 2,
+                   invalid + (size_t)b * A, NULL);
     terminal[b] = (int8_t)se_terminal(p, s);
     to_play[b] = s.to_play;
     memcpy(child_embedding + (size_t)b * sizeof(se_state), &s, sizeof(se_state));
@@ -1195,7 +1205,7 @@ long or_search_synthetic(const se_params *p, or_tree *t, uint32_t k0, uint32_t k
   int32_t *sp = (int32_t *)malloc(sizeof(int32_t) * B);
   int32_t *sa = (int32_t *)malloc(sizeof(int32_t) * B);
   uint8_t *sact = (uint8_t *)malloc(B);
-  or_synthetic_root(p, B, logits, value, qv, inv, term, tp, emb);
+  or_synthetic_root(p, B, t->lane_offset, logits, value, qv, inv, term, tp, emb);
   const uint8_t *rinv = root_invalid ? root_invalid : inv;
   or_tree_init(t, value, qv, rinv, term, tp, emb);
   long unsafe = 0;
@@ -1208,7 +1218,7 @@ long or_search_synthetic(const se_params *p, or_tree *t, uint32_t k0, uint32_t k
       memcpy(emb + (size_t)b * 16, t->embedding + ((size_t)b * t->C + parent) * 16, 16);
       sa[b] = sact[b] ? sa[b] : 0;
     }
-    or_synthetic_recurrent(p, B, sa, emb, value, qv, inv, term, tp, child_emb);
+    or_synthetic_recurrent(p, B, t->lane_offset, sa, emb, value, qv, inv, term, tp, child_emb);
     or_expand(t, i + 1, sp, sa, sact, value, qv, inv, term, tp, child_emb);
     unsafe += or_backward(t, bwd_key, sp, sa, sact, value, tp, u);
     key = next;

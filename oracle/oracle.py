@@ -82,7 +82,7 @@ class TreeStruct(C.Structure):
             "parents", "children", "to_play", "node_outcome", "node_payload",
             "edge_outcome", "edge_payload", "value_prior", "value_alpha",
             "edge_alpha", "invalid", "embedding")
-    ]
+    ] + [("lane_offset", C.c_int), ("total_batch", C.c_int)]
 
 
 class ContextSoA(C.Structure):
@@ -304,6 +304,8 @@ class Tree:
     edge_alpha: np.ndarray
     invalid_actions: np.ndarray
     embeddings: np.ndarray
+    lane_offset: int = 0
+    total_batch: int = 0
 
     @classmethod
     def empty(cls, B: int, num_nodes: int, A: int, emb_bytes: int = 0) -> "Tree":
@@ -327,7 +329,7 @@ class Tree:
             self.parents, self.children_index, self.node_to_play, self.node_categorical_outcome,
             self.node_payload, self.edge_categorical_outcome, self.edge_payload,
             self.node_value_priors, self.node_value_alpha, self.edge_alpha,
-            self.invalid_actions, self.embeddings)])
+            self.invalid_actions, self.embeddings)], self.lane_offset, self.total_batch)
 
     def summary(self) -> dict:
         B, _, A = self.dims
@@ -482,7 +484,7 @@ def synthetic_root(env: SynthParams, B: int) -> dict:
                action_values=np.zeros((B, A, 2), np.float32), invalid_actions=np.zeros((B, A), np.uint8),
                terminal_outcome=np.zeros(B, np.int8), to_play=np.zeros(B, np.int32),
                embedding=np.zeros((B, 16), np.uint8))
-    lib().or_synthetic_root(C.byref(env), C.c_int(B), *[_p(out[k]) for k in (
+    lib().or_synthetic_root(C.byref(env), C.c_int(B), C.c_int(0), *[_p(out[k]) for k in (
         "prior_logits", "value", "action_values", "invalid_actions", "terminal_outcome", "to_play",
         "embedding")])
     out["invalid_actions"] = out["invalid_actions"].astype(bool)
@@ -497,7 +499,7 @@ def synthetic_recurrent(env: SynthParams, action, parent_embedding):
                 invalid_actions=np.zeros((B, A), np.uint8), terminal_outcome=np.zeros(B, np.int8),
                 to_play=np.zeros(B, np.int32))
     child = np.zeros((B, 16), np.uint8)
-    lib().or_synthetic_recurrent(C.byref(env), C.c_int(B), _p(action),
+    lib().or_synthetic_recurrent(C.byref(env), C.c_int(B), C.c_int(0), _p(action),
                                  _p(np.ascontiguousarray(parent_embedding, np.uint8)),
                                  *[_p(step[k]) for k in ("value", "action_values", "invalid_actions",
                                                          "terminal_outcome", "to_play")], _p(child))
@@ -505,12 +507,18 @@ def synthetic_recurrent(env: SynthParams, action, parent_embedding):
 
 
 def search_synthetic(env: SynthParams, B: int, rng_key, num_simulations: int, rule: Rule,
-                     max_depth=None, policy_samples: int = 32) -> PolicyOutput:
-    """The whole search on the synthetic game, loop in C."""
+                     max_depth=None, policy_samples: int = 32, lanes: tuple[int, int] | None = None
+                     ) -> PolicyOutput:
+    """The whole search on the synthetic game, loop in C.  ``lanes=(lo, hi)``
+    runs only lanes [lo, hi) of the B-lane batch (bit-identical to the same
+    lanes of a full run); the returned arrays then hold hi - lo lanes."""
     if max_depth is None:
         max_depth = num_simulations
     A = env.num_actions
-    tree = Tree.empty(B, num_simulations + 1, A, 16)
+    lo, hi = (0, B) if lanes is None else lanes
+    tree = Tree.empty(hi - lo, num_simulations + 1, A, 16)
+    tree.lane_offset, tree.total_batch = lo, B
+    B = hi - lo
     w = np.zeros((B, A), np.float32)
     act = np.zeros(B, np.int32)
     s = tree.struct()

@@ -1,0 +1,120 @@
+"""ctypes binding of libscacchi_b200.so (the C ABI in include/scacchi_b200.h)."""
+
+from __future__ import annotations
+
+import ctypes as C
+import functools
+import os
+
+from . import _build
+
+OK, EINVAL, ECUDA = 0, 1, 2
+
+
+class ScacchiTree(C.Structure):
+    _fields_ = [("batch", C.c_int32), ("num_nodes", C.c_int32), ("num_actions", C.c_int32),
+                ("action_stride", C.c_int32), ("emb_bytes", C.c_int32)] + [
+        (n, C.c_void_p) for n in (
+            "parents", "children_index", "node_to_play", "node_outcome", "node_payload",
+            "edge_outcome", "edge_payload", "node_value_prior", "node_value_alpha", "edge_alpha",
+            "invalid", "embedding")]
+
+
+class UpdateParams(C.Structure):
+    _fields_ = [("rule", C.c_int32), ("kappa_ge_one", C.c_int32), ("inv_kappa", C.c_float),
+                ("kappa", C.c_float), ("samples", C.c_int32), ("half_width", C.c_int32),
+                ("tail_scale", C.c_float), ("min_half_range", C.c_float), ("max_half_range", C.c_float),
+                ("density_tol", C.c_float)]
+
+
+class PrefixOut(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "policy", "raw_policy", "raw_mass", "normalization_error", "finite", "grid_half_range",
+        "tail_range_clipped", "density_log_integral", "fallback_interval_count")]
+
+
+class SyntheticParams(C.Structure):
+    _fields_ = [("seed_k0", C.c_uint32), ("seed_k1", C.c_uint32), ("num_actions", C.c_int32),
+                ("legal_prob", C.c_float), ("terminal_prob", C.c_float),
+                ("degenerate_lane_prob", C.c_float), ("degenerate_alpha", C.c_float),
+                ("logc_mean", C.c_float), ("logc_std", C.c_float), ("logc_min", C.c_float),
+                ("logc_max", C.c_float)]
+
+
+class Context(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "active", "leaf_active", "leaf_action", "leaf_value", "leaf_to_play", "node_to_play",
+        "node_payload", "value_prior", "value_alpha", "edge_alpha", "edge_payload", "edge_outcome",
+        "invalid", "child_visited", "child_prior", "child_value", "child_payload", "child_outcome",
+        "child_to_play")]
+
+
+P = C.c_void_p
+I32 = C.c_int32
+F32 = C.c_float
+TREE = C.POINTER(ScacchiTree)
+
+SIGNATURES = {
+    "scacchi_tree_init": [TREE, P, P, P, P, P, P, I32, P],
+    "scacchi_simulate": [TREE, P, I32, P, P, P, P, P, P],
+    "scacchi_expand": [TREE, I32, P, P, P, P, P, P, P, P, P, I32, P],
+    "scacchi_backward": [TREE, P, P, P, P, P, P, C.POINTER(UpdateParams), P, P],
+    "scacchi_root_policy": [TREE, P, P, I32, P, P, P],
+    "scacchi_summary": [TREE, P, P, P, P, P, P, P, P],
+    "scacchi_prefix_cdf": [P, P, P, I32, I32, I32, F32, F32, F32, C.POINTER(PrefixOut), P],
+    "scacchi_posterior_best_policy": [P, P, P, P, I32, I32, I32, P, P],
+    "scacchi_thompson_sample": [P, P, P, P, I32, I32, P, P],
+    "scacchi_update_posterior": [P, C.POINTER(Context), I32, I32, C.POINTER(UpdateParams), P, P, P, P, P],
+    "scacchi_root_readout": [I32, I32, P, P, P, P, P, P, P, I32, F32, I32, F32, F32, F32, P, P, P],
+    "scacchi_synthetic_root": [C.POINTER(SyntheticParams), I32, P, P, P, P, P, P, P, P],
+    "scacchi_synthetic_evaluate": [C.POINTER(SyntheticParams), I32, P, P, P, P, P, P, P, P],
+    "scacchi_synthetic_recurrent": [C.POINTER(SyntheticParams), I32, P, P, P, P, P, P, P, P, P],
+    "scacchi_search_workspace_bytes": [I32, I32, I32],
+    "scacchi_search_synthetic": [TREE, C.POINTER(SyntheticParams), P, I32, I32, C.POINTER(UpdateParams), P, P,
+                                 P],
+    "scacchi_key_schedule": [C.c_uint32, C.c_uint32, I32, P],
+    "scacchi_split_host": [C.c_uint32, C.c_uint32, I32, P],
+    "scacchi_fold_in_host": [C.c_uint32, C.c_uint32, C.c_uint32, P],
+    "scacchi_device_error": [P],
+    "scacchi_launch_count": [],
+}
+RESTYPES = {"scacchi_search_workspace_bytes": C.c_size_t, "scacchi_launch_count": C.c_uint64}
+
+
+class ScacchiError(RuntimeError):
+    pass
+
+
+@functools.lru_cache(maxsize=None)
+def lib() -> C.CDLL:
+    """Load the in-tree CUDA library, building it first if it is missing.
+
+    There is no fallback: without the library the search cannot run.
+    """
+    path = _build.LIB
+    if not os.path.exists(path):
+        _build.build()
+    handle = C.CDLL(path)
+    for name, args in SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.argtypes = args
+        fn.restype = RESTYPES.get(name, C.c_int)
+    return handle
+
+
+def check(rc: int, what: str) -> None:
+    if rc == OK:
+        return
+    if rc == EINVAL:
+        raise ValueError(f"{what}: arguments rejected by the CUDA library")
+    raise ScacchiError(f"{what}: CUDA launch failed (status {rc})")
+
+
+def device_error() -> int:
+    flags = C.c_uint32(0)
+    check(lib().scacchi_device_error(C.byref(flags)), "scacchi_device_error")
+    return int(flags.value)
+
+
+def launch_count() -> int:
+    return int(lib().scacchi_launch_count())

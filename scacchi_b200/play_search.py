@@ -1,0 +1,281 @@
+"""The search()/evaluator boundary (scacchi/play_search.py of the reference).
+
+``make_search(env, evaluator, search_cfg)`` returns
+``search(root_state, rng_key) -> PosteriorTargets`` exactly like the
+reference; the Dirichlet-Thompson search, its root readout and target packing
+run on the GPU.  ``root_state`` follows the pgx.State fields the reference
+reads: observation, legal_action_mask, current_player, rewards, terminated.
+
+An env may provide ``native_recurrent_fn(evaluator)`` (a recurrent function
+whose ``native_search`` runs the whole simulation loop in the CUDA library)
+and ``embedding(root_state)`` (the per-node state record); otherwise the
+generic expand function below calls ``env.step`` and ``evaluator`` from
+Python once per simulation.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import functools
+from typing import Any, Callable, NamedTuple
+
+import torch
+
+from . import _lib
+from .dirichlet_mctx import RecurrentFnOutput, RootFnOutput, dirichlet_thompson_policy
+from .dirichlet_mctx.outcomes import NO_OUTCOME, align_categorical_outcome, outcome_mean, outcome_utility
+from .dirichlet_mctx.posterior_updates import (DEFAULT_POLICY_SAMPLE_CHUNK_SIZE, update_posterior,
+                                               update_posterior_prefix_cdf)
+from .dirichlet_mctx.tree import ptr, stream_handle
+from .types import (DirichletThompsonSearchConfig, MonteCarloPosteriorUpdateConfig, NumericalPosteriorUpdateConfig,
+                    PosteriorUpdateKind, QActionSet, QPairReduction, QSupervisionConfig, RootPolicySupport,
+                    SearchConfig, SearchKind)
+
+TARGET_PAD = 0
+TARGET_DIRICHLET = 1
+TARGET_CATEGORICAL = 2
+
+
+class EvaluatorOutput(NamedTuple):
+    logits: torch.Tensor
+    value: torch.Tensor | None = None
+    alpha_v: torch.Tensor | None = None
+    alpha_q: torch.Tensor | None = None
+
+
+class PosteriorPrediction(NamedTuple):
+    policy: torch.Tensor
+    value: torch.Tensor | None = None
+    alpha_v: torch.Tensor | None = None
+    alpha_q: torch.Tensor | None = None
+
+
+class QSupervision(NamedTuple):
+    selected: torch.Tensor
+    pair_weight: torch.Tensor
+
+
+class TargetMetadata(NamedTuple):
+    mask: torch.Tensor | None = None
+    q_supervision: QSupervision | None = None
+    q_positive_evidence_action: torch.Tensor | None = None
+    q_positive_policy_action: torch.Tensor | None = None
+    search_action: torch.Tensor | None = None
+    q_target_kind: torch.Tensor | None = None
+    q_target_weight: torch.Tensor | None = None
+    q_target_outcome: torch.Tensor | None = None
+    q_target_distance: torch.Tensor | None = None
+    v_target_kind: torch.Tensor | None = None
+    v_target_weight: torch.Tensor | None = None
+    v_target_outcome: torch.Tensor | None = None
+    v_target_distance: torch.Tensor | None = None
+
+
+class PosteriorTargets(NamedTuple):
+    prediction: PosteriorPrediction
+    metadata: TargetMetadata | None = None
+
+
+Search = Callable[[Any, Any], PosteriorTargets]
+
+
+def evaluator_output_from_model_output(model_output: Any) -> EvaluatorOutput:
+    """play_search.py:95-109."""
+    if isinstance(model_output, EvaluatorOutput):
+        return model_output
+    if isinstance(model_output, torch.Tensor):
+        return EvaluatorOutput(logits=model_output)
+    logits, alpha_v, alpha_q = model_output
+    return EvaluatorOutput(logits=logits, value=outcome_utility(outcome_mean(alpha_v)), alpha_v=alpha_v,
+                           alpha_q=alpha_q)
+
+
+def make_evaluator(model: Any) -> Callable[[torch.Tensor], EvaluatorOutput]:
+    """play_search.py:112-118."""
+
+    def evaluator(obs: torch.Tensor) -> EvaluatorOutput:
+        return evaluator_output_from_model_output(model(obs))
+
+    return evaluator
+
+
+def _required_output(value, name: str):
+    if value is None:
+        raise ValueError(f"evaluator output is missing {name}")
+    return value
+
+
+def terminal_outcome_from_reward(reward: torch.Tensor, num_outcomes: int = 2) -> torch.Tensor:
+    """dirichlet_q_search.py:27-40."""
+    rounded = torch.round(reward).to(torch.int32)
+    if num_outcomes == 2:
+        outcome = torch.div(rounded + 1, 2, rounding_mode="floor")
+    elif num_outcomes == 3:
+        outcome = rounded + 1
+    else:
+        raise ValueError(f"unsupported outcome count: {num_outcomes}")
+    return outcome.to(torch.int8)
+
+
+def make_dirichlet_expand_fn(env: Any, evaluator: Callable):
+    """dirichlet_q_search.py:43-76: env.step -> evaluator -> RecurrentFnOutput."""
+    if hasattr(env, "native_recurrent_fn"):
+        return env.native_recurrent_fn(evaluator)
+
+    def expand_fn(_, rng_key, action: torch.Tensor, env_state: Any):
+        del rng_key
+        parent_player = env_state.current_player
+        child = env.step(env_state, action)
+        prediction = evaluator(child.observation)
+        alpha_v = _required_output(prediction.alpha_v, "alpha_v")
+        alpha_q = _required_output(prediction.alpha_q, "alpha_q")
+        B = child.rewards.shape[0]
+        reward = child.rewards[torch.arange(B, device=child.rewards.device), parent_player.long()]
+        parent_outcome = terminal_outcome_from_reward(reward, alpha_v.shape[-1])
+        child_outcome = align_categorical_outcome(parent_outcome, parent_player, child.current_player,
+                                                  alpha_v.shape[-1])
+        terminal = torch.where(child.terminated, child_outcome, torch.full_like(child_outcome, NO_OUTCOME))
+        step = RecurrentFnOutput(value=alpha_v, action_values=alpha_q, invalid_actions=~child.legal_action_mask,
+                                 terminal_outcome=terminal, to_play=child.current_player.to(torch.int32))
+        return step, child
+
+    return expand_fn
+
+
+def _posterior_policy_sampling_budget(config) -> tuple[int, int]:
+    """play_search.py:388-404."""
+    if isinstance(config, NumericalPosteriorUpdateConfig):
+        samples, chunk = config.fallback_policy_samples, config.fallback_policy_sample_chunk_size
+    else:
+        samples, chunk = config.policy_samples, config.policy_sample_chunk_size
+    return int(samples), (max(1, int(chunk)) if chunk is not None else DEFAULT_POLICY_SAMPLE_CHUNK_SIZE)
+
+
+def _make_posterior_update(config) -> Callable:
+    """play_search.py:407-432."""
+    samples, chunk = _posterior_policy_sampling_budget(config)
+    if isinstance(config, NumericalPosteriorUpdateConfig):
+        return functools.partial(update_posterior_prefix_cdf, kappa=float(config.kappa),
+                                 half_width=int(config.half_width), tail_scale=float(config.tail_scale),
+                                 min_half_range=float(config.min_half_range),
+                                 max_half_range=float(config.max_half_range), fallback_policy_samples=samples,
+                                 fallback_policy_sample_chunk_size=chunk)
+    return functools.partial(update_posterior, kappa=float(config.kappa), policy_samples=samples,
+                             policy_sample_chunk_size=chunk)
+
+
+def build_q_supervision(action_set, reduction, q_search_count, posterior_policy_target, solved_action,
+                        legal) -> QSupervision:
+    """dirichlet_q_search.py:119-182."""
+    evidence_mass = q_search_count.sum(-1) + torch.zeros_like(posterior_policy_target)
+    positive_evidence = q_search_count.sum(-1) > 0
+    positive_policy = posterior_policy_target > 0
+    if action_set == QActionSet.positive_search_evidence_or_solved:
+        source_selected, source_weight = positive_evidence, evidence_mass
+    elif action_set == QActionSet.positive_posterior_policy_or_solved:
+        source_selected, source_weight = positive_policy, posterior_policy_target
+    else:
+        raise ValueError(f"unknown Q action set: {action_set!r}")
+    selected = legal & (source_selected | solved_action)
+    if reduction == QPairReduction.mean_over_selected_state_action_pairs:
+        pair_weight = selected.to(posterior_policy_target.dtype)
+    elif reduction == QPairReduction.legacy_normalized_source_weighted_mean:
+        pair_weight = torch.where(legal & solved_action, torch.clamp(source_weight, min=1.0), source_weight)
+        pair_weight = torch.where(selected, pair_weight, torch.zeros_like(pair_weight))
+    else:
+        raise ValueError(f"unknown Q pair reduction: {reduction!r}")
+    return QSupervision(selected=selected, pair_weight=pair_weight)
+
+
+def dirichlet_root_policy_readout(native_policy: torch.Tensor, summary, legal_action_mask: torch.Tensor,
+                                  search_cfg: DirichletThompsonSearchConfig) -> torch.Tensor:
+    """play_search.py:298-364 (numerical update kind; the Monte Carlo kind
+    returns the native policy unchanged)."""
+    if search_cfg.posterior_update.kind != PosteriorUpdateKind.numerical:
+        return native_policy
+    num = search_cfg.posterior_update.numerical
+    B, A = native_policy.shape
+    dev = native_policy.device
+    target = torch.empty((B, A), dtype=torch.float32, device=dev)
+    legal = legal_action_mask.to(torch.uint8).contiguous()
+    _lib.check(_lib.lib().scacchi_root_readout(
+        B, A, ptr(native_policy.contiguous()), ptr(summary.visit_counts), ptr(summary.alpha),
+        ptr(summary.q_categorical_outcome), ptr(summary.q_categorical_distance), ptr(summary.v_categorical_outcome),
+        ptr(legal), int(search_cfg.root_policy_support == RootPolicySupport.search_evidence),
+        float(search_cfg.policy_target_temperature), int(num.half_width), float(num.tail_scale),
+        float(num.min_half_range), float(num.max_half_range), ptr(target), None, stream_handle(dev)),
+        "root_readout")
+    return target
+
+
+def run_dirichlet_thompson_search(env_state, prediction: EvaluatorOutput, expand_fn, rng_key,
+                                  search_cfg: DirichletThompsonSearchConfig,
+                                  q_supervision_config: QSupervisionConfig, embedding: Any = None,
+                                  stats: torch.Tensor | None = None) -> PosteriorTargets:
+    """play_search.py:435-548."""
+    alpha_v = _required_output(prediction.alpha_v, "alpha_v")
+    alpha_q = _required_output(prediction.alpha_q, "alpha_q")
+    B = env_state.rewards.shape[0]
+    dev = alpha_v.device
+    player = env_state.current_player.long()
+    root_reward = env_state.rewards[torch.arange(B, device=dev), player]
+    root_terminal = torch.where(env_state.terminated, terminal_outcome_from_reward(root_reward, alpha_v.shape[-1]),
+                                torch.full((B,), NO_OUTCOME, dtype=torch.int8, device=dev))
+    root = RootFnOutput(prior_logits=prediction.logits, value=alpha_v, action_values=alpha_q,
+                        embedding=env_state if embedding is None else embedding, terminal_outcome=root_terminal,
+                        to_play=env_state.current_player.to(torch.int32))
+    update_cfg = search_cfg.posterior_update.active()
+    samples, chunk = _posterior_policy_sampling_budget(update_cfg)
+    legal = env_state.legal_action_mask
+    out = dirichlet_thompson_policy((), rng_key, root=root, recurrent_fn=expand_fn,
+                                    num_simulations=int(search_cfg.num_simulations), invalid_actions=~legal,
+                                    posterior_update=_make_posterior_update(update_cfg),
+                                    max_depth=search_cfg.max_depth, policy_samples=samples,
+                                    policy_sample_chunk_size=chunk, stats=stats)
+    summary = out.search_tree.summary()
+    policy_target = dirichlet_root_policy_readout(out.action_weights, summary, legal, search_cfg)
+    beta_q, beta_v = summary.alpha, summary.value_alpha
+    q_count = summary.visit_counts[..., None]
+    q_cat = summary.q_categorical_outcome != NO_OUTCOME
+    v_cat = summary.v_categorical_outcome != NO_OUTCOME
+    i8 = dict(dtype=torch.int8, device=dev)
+    q_kind = torch.where(legal, torch.where(q_cat, torch.full_like(q_cat, TARGET_CATEGORICAL, **i8),
+                                            torch.full_like(q_cat, TARGET_DIRICHLET, **i8)),
+                         torch.full_like(q_cat, TARGET_PAD, **i8))
+    v_kind = torch.where(v_cat, torch.full_like(v_cat, TARGET_CATEGORICAL, **i8),
+                         torch.full_like(v_cat, TARGET_DIRICHLET, **i8))
+    q_sup = build_q_supervision(q_supervision_config.action_set, q_supervision_config.reduction, q_count,
+                                policy_target, q_cat, legal)
+    metadata = TargetMetadata(
+        mask=policy_target.sum(-1) > 0, q_supervision=q_sup,
+        q_positive_evidence_action=legal & (q_count.sum(-1) > 0), q_positive_policy_action=legal & (policy_target > 0),
+        search_action=out.action, q_target_kind=q_kind, q_target_weight=legal.to(beta_q.dtype),
+        q_target_outcome=summary.q_categorical_outcome, q_target_distance=summary.q_categorical_distance,
+        v_target_kind=v_kind, v_target_weight=torch.ones_like(summary.v_categorical_distance, dtype=beta_v.dtype),
+        v_target_outcome=summary.v_categorical_outcome, v_target_distance=summary.v_categorical_distance)
+    return PosteriorTargets(prediction=PosteriorPrediction(policy=policy_target, alpha_v=beta_v, alpha_q=beta_q),
+                            metadata=metadata)
+
+
+def make_search(env, evaluator: Callable, search_cfg: SearchConfig | DirichletThompsonSearchConfig,
+                q_supervision_config: QSupervisionConfig | None = None,
+                stats: torch.Tensor | None = None) -> Search:
+    """play_search.py:609-624 for the dirichlet_thompson kind."""
+    if q_supervision_config is None:
+        q_supervision_config = QSupervisionConfig()
+    if isinstance(search_cfg, SearchConfig):
+        if search_cfg.kind != SearchKind.dirichlet_thompson:
+            raise ValueError(f"search kind {search_cfg.kind!s} is not implemented on this backend; "
+                             "use dirichlet_thompson")
+        search_cfg = search_cfg.dirichlet_thompson
+    expand_fn = make_dirichlet_expand_fn(env, evaluator)
+    embed = getattr(env, "embedding", None)
+
+    def search(root_state, rng_key) -> PosteriorTargets:
+        prediction = evaluator(root_state.observation)
+        return run_dirichlet_thompson_search(root_state, prediction, expand_fn, rng_key, search_cfg,
+                                             q_supervision_config,
+                                             embedding=embed(root_state) if embed is not None else None,
+                                             stats=stats)
+
+    return search

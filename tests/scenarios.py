@@ -292,3 +292,67 @@ SCENARIOS = [
         num_simulations=2, invalid_actions=np.array([[False, True]]), policy_samples=8,
         check=_expand_terminal_check),
 ]
+
+
+def _alternating_chain_step(terminal_depth):
+    """recurrent_fn of tests/test_dirichlet_mctx_categorical.py:203-227 with
+    binary outcomes (win index 1): the terminal child is a certified loss for
+    its player and the players alternate by depth."""
+
+    def step(action, depth):
+        child = depth + 1
+        B = child.shape[0]
+        td = np.broadcast_to(np.asarray(terminal_depth), (B,))
+        terminal = child >= td
+        return dict(
+            value=np.ones((B, 2), np.float32),
+            action_values=np.ones((B, 1, 2), np.float32),
+            invalid_actions=terminal[:, None].copy(),
+            terminal_outcome=np.where(terminal, 0, NO_OUTCOME).astype(np.int8),
+            to_play=(child % 2).astype(np.int32),
+        ), child
+
+    return step
+
+
+def _terminal_chain_check(out):
+    # tests/test_dirichlet_mctx_categorical.py:242-272 (win index 2 -> 1)
+    tree = out.tree
+    assert np.array_equal(tree.node_categorical_outcome[0, :4], [1, 0, 1, 0])
+    assert np.array_equal(tree.node_payload[0, :4], [3, 2, 1, 0])
+    assert np.array_equal(tree.edge_categorical_outcome[0, :3, 0], [1, 0, 1])
+    assert np.array_equal(tree.edge_payload[0, :3, 0], [3, 2, 1])
+    assert np.array_equal(tree.parents[0], [-1, 0, 1, 2, -1, -1, -1, -1])
+    assert out.action[0] == 0
+    assert np.array_equal(out.action_weights, [[1.0]])
+    s = tree.summary()
+    assert s["v_categorical_outcome"][0] == 1
+    assert s["v_categorical_distance"][0] == 3
+    assert s["q_categorical_outcome"][0, 0] == 1
+    assert s["q_categorical_distance"][0, 0] == 3
+
+
+def _frozen_lane_check(out):
+    # tests/test_dirichlet_mctx_categorical.py:325-342
+    tree = out.tree
+    assert np.array_equal(tree.node_categorical_outcome[:, 0], [1, 1])
+    assert np.array_equal(tree.node_payload[:, 0], [1, 3])
+    assert np.array_equal(tree.parents[0], [-1, 0, -1, -1, -1, -1])
+    assert np.array_equal(tree.parents[1], [-1, 0, 1, 2, -1, -1])
+    assert np.array_equal(out.action_weights, np.ones((2, 1)))
+
+
+SCENARIOS += [
+    Scenario(
+        "terminal_chain_perspective_and_distance",  # test_dirichlet_mctx_categorical.py:203-272
+        make_root([[1.0, 1.0]]),
+        _alternating_chain_step(3),
+        num_simulations=7, invalid_actions=np.array([[False]]), max_depth=7, policy_samples=4,
+        rng_key=prng_key(11), check=_terminal_chain_check),
+    Scenario(
+        "solved_lane_stays_frozen",  # test_dirichlet_mctx_categorical.py:274-342
+        make_root([[[1.0, 1.0]], [[1.0, 1.0]]]),
+        _alternating_chain_step(np.array([1, 3])),
+        num_simulations=5, invalid_actions=np.zeros((2, 1), bool), max_depth=5, policy_samples=4,
+        rng_key=prng_key(17), check=_frozen_lane_check),
+]
