@@ -1206,7 +1206,9 @@ long or_search_synthetic(const se_params *p, or_tree *t, uint32_t k0, uint32_t k
   int32_t *sa = (int32_t *)malloc(sizeof(int32_t) * B);
   uint8_t *sact = (uint8_t *)malloc(B);
   or_synthetic_root(p, B, t->lane_offset, logits, value, qv, inv, term, tp, emb);
-  const uint8_t *rinv = root_invalid ? root_invalid : inv;
+  /* the root mask must outlive the loop, which reuses `inv` for each step */
+  uint8_t *rinv = (uint8_t *)malloc((size_t)B * A);
+  memcpy(rinv, root_invalid ? root_invalid : inv, (size_t)B * A);
   or_tree_init(t, value, qv, rinv, term, tp, emb);
   long unsafe = 0;
   sk_key key = search_key;
@@ -1224,6 +1226,7 @@ long or_search_synthetic(const se_params *p, or_tree *t, uint32_t k0, uint32_t k
     key = next;
   }
   or_root_policy(t, policy_key, rinv, policy_samples, weights, action);
+  free(rinv);
   free(logits);
   free(value);
   free(qv);

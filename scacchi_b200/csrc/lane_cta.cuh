@@ -1,0 +1,665 @@
+// One CTA per search lane, one action per thread (W = ceil(A / 32) warps).
+//
+// The descent and the bottom-up repair walk a lane's tree one node at a
+// time, so their latency per node bounds the whole launch: a few deep lanes
+// finish long after the rest.  Spreading a node's actions over W warps cuts
+// that latency by W against the warp-per-lane mapping.  Reductions over
+// actions keep the canonical order (partial sums v[t] + v[t+32] + v[t+64] +
+// v[t+96], then the xor butterfly), computed by warp 0 from shared memory.
+//
+// The quadrature grid's per-(action, point) values live in shared-memory
+// matrices [Q][32W] so each grid point's sum over actions is one warp's
+// column reduction, and the estimator's guards are evaluated after the
+// density normalisation: when they already force the Monte Carlo fallback,
+// the remaining prefix-CDF passes are skipped (their policy is discarded).
+//
+// Included inside search.cu's anonymous namespace.
+
+template <int W>
+struct Cta {
+  static constexpr int kT = 32 * W;
+  float *red;        // [4][kT] reduction inputs
+  float *bc;         // [16] broadcast results
+  float *pv;         // [W] per-warp argmax values
+  int *pi;           // [W] per-warp argmax indices
+  float *lx, *l1mx, *lj, *flp, *joint, *score;  // [Q]
+  float *zc;         // [Q] zero counts (exact small integers)
+  float *D, *F, *X, *Z;  // [Q][kT]
+  int Q;
+};
+
+template <int W>
+__host__ __device__ constexpr size_t cta_smem_floats(int Q) {
+  return (size_t)4 * Cta<W>::kT + 16 + 2 * W + 7 * (size_t)Q + 4 * (size_t)Q * Cta<W>::kT;
+}
+
+template <int W>
+__device__ __forceinline__ Cta<W> cta_scratch(int Q) {
+  extern __shared__ float smem[];
+  Cta<W> c;
+  float *p = smem;
+  c.red = p;
+  p += 4 * Cta<W>::kT;
+  c.bc = p;
+  p += 16;
+  c.pv = p;
+  p += W;
+  c.pi = reinterpret_cast<int *>(p);
+  p += W;
+  c.lx = p;
+  c.l1mx = p + Q;
+  c.lj = p + 2 * Q;
+  c.flp = p + 3 * Q;
+  c.joint = p + 4 * Q;
+  c.score = p + 5 * Q;
+  c.zc = p + 6 * Q;
+  p += 7 * Q;
+  c.D = p;
+  c.F = p + (size_t)Q * Cta<W>::kT;
+  c.X = p + 2 * (size_t)Q * Cta<W>::kT;
+  c.Z = p + 3 * (size_t)Q * Cta<W>::kT;
+  c.Q = Q;
+  return c;
+}
+
+// canonical sum of column `col` (length A) of a [*, kT] matrix, by one warp
+template <int W>
+__device__ __forceinline__ float column_sum(const float *col, int A, int lane) {
+  float p = 0.0f;
+  bool first = true;
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    const int a = lane + kWarp * j;
+    if (a < A) {
+      p = first ? col[a] : p + col[a];
+      first = false;
+    }
+  }
+  return butterfly_sum(p);
+}
+
+// Up to 4 simultaneous canonical sums over actions; every thread gets them.
+template <int W, int K>
+__device__ __forceinline__ void cta_sums(const Cta<W> &c, const float (&v)[K], float (&out)[K], int A) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+#pragma unroll
+  for (int k = 0; k < K; ++k) c.red[k * Cta<W>::kT + t] = v[k];
+  __syncthreads();
+  for (int kk = warp; kk < K; kk += W) {
+    const float s = column_sum<W>(c.red + kk * Cta<W>::kT, A, lane);
+    if (lane == 0) c.bc[kk] = s;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < K; ++k) out[k] = c.bc[k];
+  __syncthreads();
+}
+
+template <int W>
+__device__ __forceinline__ float cta_sum(const Cta<W> &c, float v, int A) {
+  float in[1] = {v}, out[1];
+  cta_sums<W, 1>(c, in, out, A);
+  return out[0];
+}
+
+// argmax over a per-thread value (thread index = action index), with the
+// jnp.argmax order of `beats`
+template <int W>
+__device__ __forceinline__ int cta_argmax_by_action(const Cta<W> &c, float v, int A) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const float vv = t < A ? v : -SM_INF;
+  const int ii = t < A ? t : INT_MAX;
+  c.red[3 * Cta<W>::kT + t] = vv;
+  const int wi = warp_argmax(vv, ii);
+  if (lane == 0) c.pi[warp] = wi;
+  __syncthreads();
+  float bv = -SM_INF;
+  int bi = INT_MAX;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const int i = c.pi[w];
+    const float val = i == INT_MAX ? -SM_INF : c.red[3 * Cta<W>::kT + i];
+    if (beats(val, i, bv, bi)) {
+      bv = val;
+      bi = i;
+    }
+  }
+  __syncthreads();
+  return bi;
+}
+
+template <int W>
+__device__ __forceinline__ int cta_reduce_add(const Cta<W> &c, int v) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const int s = __reduce_add_sync(kFull, v);
+  if (lane == 0) c.pi[warp] = s;
+  __syncthreads();
+  int total = 0;
+#pragma unroll
+  for (int w = 0; w < W; ++w) total += c.pi[w];
+  __syncthreads();
+  return total;
+}
+
+template <int W>
+__device__ __forceinline__ int cta_reduce_min(const Cta<W> &c, int v) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const int s = __reduce_min_sync(kFull, v);
+  if (lane == 0) c.pi[warp] = s;
+  __syncthreads();
+  int m = c.pi[0];
+#pragma unroll
+  for (int w = 1; w < W; ++w) m = c.pi[w] < m ? c.pi[w] : m;
+  __syncthreads();
+  return m;
+}
+
+template <int W>
+__device__ __forceinline__ int cta_reduce_max(const Cta<W> &c, int v) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const int s = __reduce_max_sync(kFull, v);
+  if (lane == 0) c.pi[warp] = s;
+  __syncthreads();
+  int m = c.pi[0];
+#pragma unroll
+  for (int w = 1; w < W; ++w) m = c.pi[w] > m ? c.pi[w] : m;
+  __syncthreads();
+  return m;
+}
+
+// exact float min/max (order independent; NaN never wins, as in the oracle)
+template <int W>
+__device__ __forceinline__ float cta_min_float(const Cta<W> &c, float v) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const float s = warp_min_float(v);
+  if (lane == 0) c.pv[warp] = s;
+  __syncthreads();
+  float m = c.pv[0];
+#pragma unroll
+  for (int w = 1; w < W; ++w) m = c.pv[w] < m ? c.pv[w] : m;
+  __syncthreads();
+  return m;
+}
+
+template <int W>
+__device__ __forceinline__ float cta_max_float(const Cta<W> &c, float v) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const float s = warp_max_float(v);
+  if (lane == 0) c.pv[warp] = s;
+  __syncthreads();
+  float m = c.pv[0];
+#pragma unroll
+  for (int w = 1; w < W; ++w) m = c.pv[w] > m ? c.pv[w] : m;
+  __syncthreads();
+  return m;
+}
+
+// thompson_sample (action_selection.py:135-143) with one action per thread
+template <int W>
+__device__ int cta_thompson(const Cta<W> &c, sk_key key, const GammaShape &g0, const GammaShape &g1, bool masked,
+                            int8_t cat, bool use_cat, int A, uint64_t lane_base, uint64_t stride) {
+  const int a = threadIdx.x;
+  float u = -SM_INF;
+  if (a < A && !masked) {
+    if (use_cat && cat != kNoOutcome) {
+      u = cat == 1 ? 1.0f : (cat == 0 ? -1.0f : 0.0f);
+    } else {
+      const DrawKeys k = draw_keys(key);
+      const uint64_t base = lane_base + (uint64_t)a * 2u;
+      const float lg0 = log_gamma_draw(k, base, stride, g0);
+      const float lg1 = log_gamma_draw(k, base + 1, stride, g1);
+      u = binary_utility(lg0, lg1);
+    }
+  }
+  return cta_argmax_by_action<W>(c, u, A);
+}
+
+// posterior_best_policy (action_selection.py:146-194), one action per thread
+template <int W>
+__device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, bool invalid, int8_t cat,
+                               bool use_cat, int S, int A, int b, int B) {
+  const int a = threadIdx.x;
+  const bool present = a < A;
+  const uint64_t lane_base = (uint64_t)b * A * 2u, stride = (uint64_t)B * A * 2u;
+  GammaShape g0 = gamma_shape(1.0f), g1 = g0;
+  if (present && !invalid && !(use_cat && cat != kNoOutcome)) {
+    g0 = gamma_shape(a0);
+    g1 = gamma_shape(a1);
+  }
+  if (S == 1) {
+    const int best = cta_thompson<W>(c, key, g0, g1, invalid, cat, use_cat, A, lane_base, stride);
+    return (present && !invalid && a == best) ? 1.0f : 0.0f;
+  }
+  const sk_key sample_key = sk_split(key, 0);
+  float hits = 0.0f;
+  for (int s = 0; s < S; ++s) {
+    const int best =
+        cta_thompson<W>(c, sk_split(sample_key, (uint64_t)s), g0, g1, invalid, cat, use_cat, A, lane_base, stride);
+    if (a == best) hits = hits + 1.0f;
+  }
+  const int legal = __syncthreads_count(present && !invalid);
+  float policy = (present && !invalid) ? hits / (float)S : 0.0f;
+  const float total = cta_sum<W>(c, policy, A);
+  const float denom = total > 1.0f ? total : 1.0f;
+  const float lc = (float)(legal > 1 ? legal : 1);
+  return total > 0.0f ? policy / denom : (invalid ? 0.0f : 1.0f) / lc;
+}
+
+struct PrefixResult1 {
+  float policy;  // this thread's action
+  bool unsafe;   // clipped, non-finite or density error above tolerance
+};
+
+// binary_posterior_best_policy_prefix_quadrature (prefix_cdf.py:217-445) and
+// the guard of update_posterior_prefix_cdf (posterior_updates.py:282-290),
+// one action per thread.  Returns early with unsafe = true as soon as the
+// clipping or density guard fires.
+template <int W>
+__device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1, bool invalid, int8_t outc, int A,
+                                            const PrefixParams &P, float tol) {
+  const int a = threadIdx.x, lane = a % kWarp, warp = a / kWarp;
+  const int h = P.h, Q = 2 * h + 1;
+  const int T = Cta<W>::kT;
+  const bool present = a < A;
+  const bool legal = present && !invalid;
+  const bool unres = legal && outc == kNoOutcome;
+  const bool cwin = legal && outc == 1;
+  const int n_unres = __syncthreads_count(unres);
+  const bool has_unres = n_unres > 0;
+  const bool has_legal = __syncthreads_or(legal);
+  const bool has_cw = __syncthreads_or(cwin);
+  float amin = SM_INF;
+  if (unres) {
+    const float v0 = a0 > SM_TINY ? a0 : SM_TINY;
+    const float v1 = a1 > SM_TINY ? a1 : SM_TINY;
+    amin = v0 < v1 ? v0 : v1;
+  }
+  amin = cta_min_float<W>(c, amin);
+  float requested = sm_asinhf_pos(P.tail / amin);
+  if (!has_unres) requested = P.min_hr;
+  float hr = requested;
+  if (hr < P.min_hr) hr = P.min_hr;
+  if (hr > P.max_hr) hr = P.max_hr;
+  const bool clipped = has_unres && requested > P.max_hr;
+  PrefixResult1 r;
+  r.policy = 0.0f;
+  r.unsafe = clipped;
+  if (clipped) return r;
+  const float fh = (float)h;
+  for (int k = a; k < Q; k += T) {
+    const float unit = (float)(k - h) / fh;
+    const float coord = hr * unit;
+    const float logit = sm_sinhf(coord);
+    c.lx[k] = -sm_softplusf(-logit);
+    c.l1mx[k] = -sm_softplusf(logit);
+    c.lj[k] = log_cosh(coord);
+  }
+  __syncthreads();
+  const float hstep = 0.5f * (hr / fh);
+  // density normalisation of this action
+  const float w = unres ? (a1 > SM_TINY ? a1 : SM_TINY) : 1.0f;
+  const float l = unres ? (a0 > SM_TINY ? a0 : SM_TINY) : 1.0f;
+  const float bl = sm_betalnf(w, l);
+  float scale = -SM_INF;
+  bool nan = false;
+  for (int k = 0; k < Q; ++k) {
+    const float ld = ((w * c.lx[k] + l * c.l1mx[k]) - bl) + c.lj[k];
+    c.D[k * T + a] = ld;
+    nan |= ld != ld;
+    if (ld > scale) scale = ld;
+  }
+  if (nan) scale = SM_NAN;
+  float run = 0.0f, prev = 0.0f;
+  for (int k = 0; k < Q; ++k) {
+    const float d = unres ? sm_expf(c.D[k * T + a] - scale) : 0.0f;
+    c.D[k * T + a] = d;
+    if (k > 0) run = run + hstep * (prev + d);
+    prev = d;
+  }
+  const float dli = unres ? scale + sm_logf(run) : 0.0f;
+  const float safe = run > 0.0f ? run : 1.0f;
+  // guards available now: non-finite log-integral or |log-integral| > tol
+  const float adli = fabsf(dli);
+  const bool dnan = __syncthreads_or(present && adli != adli);
+  const bool dinf = __syncthreads_or(unres && !sm_isfinite(dli));
+  const float derr = cta_max_float<W>(c, present ? adli : 0.0f);
+  if (dinf || (!dnan && derr > tol)) {
+    r.unsafe = true;
+    return r;
+  }
+  // per grid point: leave-one-out products and the joint maximum CDF
+  run = 0.0f;
+  for (int k = 0; k < Q; ++k) {
+    const float d = c.D[k * T + a];
+    if (k > 0) run = run + hstep * (c.D[(k - 1) * T + a] + d);
+    const float cd = run / safe;
+    const bool pos = cd > 0.0f;
+    const float f = pos ? sm_logf(cd) : 0.0f;
+    const float m = f < 0.0f ? f : 0.0f;
+    c.F[k * T + a] = f;
+    c.X[k * T + a] = unres ? (pos ? m : -SM_INF) : 0.0f;
+    c.Z[k * T + a] = (unres && !pos) ? 1.0f : 0.0f;
+  }
+  __syncthreads();
+  for (int k = warp; k < Q; k += W) {
+    const float flp = column_sum<W>(c.F + k * T, A, lane);
+    const float lsum = column_sum<W>(c.X + k * T, A, lane);
+    const float z = column_sum<W>(c.Z + k * T, A, lane);
+    if (lane == 0) {
+      c.flp[k] = flp;
+      c.joint[k] = sm_expf(lsum);
+      c.zc[k] = z;
+    }
+  }
+  __syncthreads();
+  if (a == 0) {
+    c.joint[0] = has_unres ? 0.0f : 1.0f;
+    c.joint[Q - 1] = 1.0f;
+    for (int k = 1; k < Q; ++k) {
+      const float p = c.joint[k - 1], cur = c.joint[k];
+      if (p != p || (cur == cur && p > cur)) c.joint[k] = p;
+    }
+    c.joint[Q - 1] = 1.0f;
+  }
+  // winner contributions per interval
+  run = 0.0f;
+  float prev_int = 0.0f;
+  for (int k = 0; k < Q; ++k) {
+    const float d = c.D[k * T + a];
+    if (k > 0) run = run + hstep * (c.D[(k - 1) * T + a] + d);
+    const float cd = run / safe;
+    const bool pos = cd > 0.0f;
+    const int zf = unres && !pos;
+    const float f = c.F[k * T + a];
+    const float olp = ((int)c.zc[k] - zf) > 0 ? -SM_INF : c.flp[k] - f;
+    const float integ = (d / safe) * sm_expf(olp);
+    if (k > 0) {
+      const float cc = hstep * (prev_int + integ);
+      c.X[(k - 1) * T + a] = cc > 0.0f ? cc : (cc != cc ? cc : 0.0f);
+    }
+    prev_int = integ;
+  }
+  __syncthreads();
+  for (int j = warp; j < Q - 1; j += W) {
+    const float sc = column_sum<W>(c.X + j * T, A, lane);
+    if (lane == 0) c.score[j] = sc;
+  }
+  __syncthreads();
+  const float uden = (float)(n_unres > 1 ? n_unres : 1);
+  float prob = 0.0f;
+  for (int j = 0; j < Q - 1; ++j) {
+    float jinc = c.joint[j + 1] - c.joint[j];
+    jinc = jinc > 0.0f ? jinc : (jinc != jinc ? jinc : 0.0f);
+    const float sc = c.score[j];
+    const float wgt = sc > 0.0f ? c.X[j * T + a] / sc : (unres ? 1.0f : 0.0f) / uden;
+    prob = prob + wgt * jinc;
+  }
+  // _finalize_policy, prefix_cdf.py:121-183
+  const int first_cw = cta_reduce_min<W>(c, cwin ? a : INT_MAX);
+  const float cs = legal ? (float)outc : -SM_INF;
+  const int cbest = has_cw ? first_cw : cta_argmax_by_action<W>(c, cs, A);
+  float raw = (has_cw || !has_unres) ? (a == cbest ? 1.0f : 0.0f) : (unres ? prob : 0.0f);
+  raw = legal ? raw : 0.0f;
+  const float mass = cta_sum<W>(c, raw, A);
+  const float nerr = fabsf(mass - (has_legal ? 1.0f : 0.0f));
+  const float smass = mass > 0.0f ? mass : 1.0f;
+  float p = raw / smass;
+  p = has_legal ? p : 0.0f;
+  const bool fin_local = !present || (sm_isfinite(p) && sm_isfinite(raw));
+  const bool finite = __syncthreads_and(fin_local) && sm_isfinite(mass) && sm_isfinite(nerr) && sm_isfinite(hr);
+  r.policy = p;
+  r.unsafe = !finite;
+  return r;
+}
+
+// simulate / _simulate_one (search.py:21-78), one CTA per lane
+template <int W>
+__global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint32_t *key, int max_depth,
+                                                              int32_t *out_parent, int32_t *out_action,
+                                                              uint8_t *out_active, uint8_t *parent_emb,
+                                                              unsigned long long *stats) {
+  const int b = blockIdx.x, a = threadIdx.x;
+  const Cta<W> c = cta_scratch<W>(1);
+  const int A = T.A;
+  const bool present = a < A;
+  const sk_key sim_key = {key[0], key[1]};
+  sk_key k = sk_split(sim_key, (uint64_t)b);
+  auto searchable = [&](int n) {
+    bool s = false;
+    if (present) {
+      const size_t e = T.edge(b, n, a);
+      s = !T.invalid[e] && T.edge_outcome[e] == kNoOutcome;
+    }
+    return __syncthreads_or(s) != 0;
+  };
+  const bool root_active = T.node_outcome[T.node(b, 0)] == kNoOutcome && searchable(0);
+  int node = 0, next = 0, action = 0, depth = 0;
+  bool cont = root_active;
+  const uint64_t stride = (uint64_t)A * 2u;
+  unsigned long long visited_nodes = 0;
+  int prior_gathers = 0;
+  while (cont) {
+    visited_nodes += 1;
+    const sk_key next_key = sk_split(k, 0), sel_key = sk_split(k, 1);
+    node = next;
+    const int player = T.to_play[T.node(b, node)];
+    bool masked = true;
+    GammaShape g0 = gamma_shape(1.0f), g1 = g0;
+    if (present) {
+      const size_t e = T.edge(b, node, a);
+      masked = T.invalid[e] || T.edge_outcome[e] != kNoOutcome;
+      if (!masked) {
+        const int child = T.children[e];
+        float2 alpha;
+        if (child != -1 && T.edge_payload[e] <= 0 && T.ok(child)) {
+          const size_t ci = T.node(b, child);
+          alpha = align2(T.value_prior[ci], T.to_play[ci], player);
+          prior_gathers += 1;
+        } else {
+          alpha = T.edge_alpha[e];
+        }
+        g0 = gamma_shape(alpha.x);
+        g1 = gamma_shape(alpha.y);
+      }
+    }
+    action = cta_thompson<W>(c, sel_key, g0, g1, masked, kNoOutcome, false, A, 0, stride);
+    int child = T.children[T.edge(b, node, action)];
+    if (child != -1 && !T.ok(child)) child = -1;
+    const bool visited = child != -1;
+    const int safe = visited ? child : 0;
+    depth += 1;
+    const bool selectable = T.node_outcome[T.node(b, safe)] == kNoOutcome && searchable(safe);
+    cont = visited && selectable && depth < max_depth;
+    next = child;
+    k = next_key;
+  }
+  if (a == 0) {
+    out_parent[b] = node;
+    out_action[b] = action;
+    out_active[b] = root_active;
+  }
+  if (stats) {
+    const int pg = cta_reduce_add<W>(c, prior_gathers);
+    if (a == 0) {
+      atomicAdd(stats + 0, visited_nodes);
+      atomicAdd(stats + 1, (unsigned long long)pg);
+    }
+  }
+  if (parent_emb) {
+    const int p = root_active ? node : 0;
+    const uint8_t *src = T.embedding + T.node(b, p) * T.E;
+    for (int i = a; i < T.E; i += 32 * W) parent_emb[(size_t)b * T.E + i] = src[i];
+  }
+}
+
+// backward (search.py:146-171) with the built-in rules, one CTA per lane
+template <int W>
+__global__ void __launch_bounds__(32 * W) backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent,
+                                                              const int32_t *sim_action, const uint8_t *sim_active,
+                                                              const float2 *step_value, const int32_t *step_tp,
+                                                              UpdateParams P, unsigned long long *stats) {
+  const int b = blockIdx.x, a = threadIdx.x;
+  const Cta<W> c = cta_scratch<W>(P.rule == 1 ? 2 * P.prefix.h + 1 : 1);
+  const int A = T.A;
+  const bool present = a < A;
+  bool active = sim_active[b] != 0;
+  int node = active ? sim_parent[b] : 0;
+  if (!T.ok(node)) return;
+  bool leaf_active = active;
+  sk_key k = {key[0], key[1]};
+  const int leaf_action_raw = sim_action[b];
+  const int leaf_action = leaf_action_raw < 0 ? leaf_action_raw + A : leaf_action_raw;
+  const float2 leaf_value = step_value[b];
+  const int leaf_tp = step_tp[b];
+  unsigned long long unsafe_n = 0, nodes = 0, child_gathers = 0;
+  for (int level = 0; active && level < T.C; ++level) {
+    const sk_key next_key = sk_split(k, 0), update_key = sk_split(k, 1);
+    const size_t ni = T.node(b, node);
+    const int node_tp = T.to_play[ni];
+    const int node_payload = T.node_payload[ni];
+    const float2 vprior = T.value_prior[ni], valpha = T.value_alpha[ni];
+    const int8_t node_outcome = T.node_outcome[ni];
+    // gather this thread's action (utils.py:35-50)
+    float2 ea = make_float2(1.0f, 1.0f);
+    int ep = 0;
+    int8_t eo = kNoOutcome;
+    bool inv = true, cvis = false;
+    float2 cprior = ea, cvalue = ea;
+    int cpay = 0, ctp = 0;
+    int8_t cout = kNoOutcome;
+    size_t e = 0;
+    if (present) {
+      e = T.edge(b, node, a);
+      ea = T.edge_alpha[e];
+      ep = T.edge_payload[e];
+      eo = T.edge_outcome[e];
+      inv = T.invalid[e] != 0;
+      int child = T.children[e];
+      cvis = child != -1;
+      if (child != -1 && !T.ok(child)) child = -1;
+      const size_t ci = T.node(b, child != -1 ? child : 0);
+      cprior = T.value_prior[ci];
+      cvalue = T.value_alpha[ci];
+      cpay = T.node_payload[ci];
+      cout = T.node_outcome[ci];
+      ctp = T.to_play[ci];
+    }
+    // _repair_inputs, posterior_updates.py:66-190
+    const bool unresolved = eo == kNoOutcome;
+    float e0 = ea.x, e1 = ea.y;
+    int nep = ep;
+    if (leaf_active && a == leaf_action && unresolved) {
+      const float2 d = align2(leaf_value, leaf_tp, node_tp);
+      e0 = d.x;
+      e1 = d.y;
+      nep = nep + 1;
+    }
+    if (cvis && cout == kNoOutcome && cpay > 0 && unresolved) {
+      const float2 cv = align2(cvalue, ctp, node_tp);
+      e0 = cv.x;
+      e1 = cv.y;
+      nep = 1 + cpay;
+    }
+    float eff0 = e0, eff1 = e1;
+    if (cvis && unresolved && nep <= 0) {
+      const float2 cp = align2(cprior, ctp, node_tp);
+      eff0 = cp.x;
+      eff1 = cp.y;
+    }
+    float cache0 = eff0, cache1 = eff1;
+    if (!unresolved) {
+      const float s = eff0 + eff1;
+      cache0 = s * (eo == 0 ? 1.0f : 0.0f);
+      cache1 = s * (eo == 1 ? 1.0f : 0.0f);
+    }
+    const int delta = cta_reduce_add<W>(c, (present && unresolved && !inv) ? nep - ep : 0);
+    const int n_down = node_payload + delta;
+    // search policy: guarded prefix-CDF or Monte Carlo
+    float policy = 0.0f;
+    bool unsafe = false;
+    if (P.rule == 1) {
+      const PrefixResult1 pr = cta_prefix_guarded<W>(c, eff0, eff1, inv, eo, A, P.prefix, P.density_tol);
+      policy = pr.policy;
+      unsafe = pr.unsafe;
+    }
+    if (P.rule != 1 || unsafe)
+      policy = cta_mc_policy<W>(c, update_key, eff0, eff1, inv, eo, true, P.samples, A, b, T.B);
+    // mix_value_prior, posterior_updates.py:40-63
+    float in2[2] = {policy * cache0, policy * cache1}, w2[2];
+    cta_sums<W, 2>(c, in2, w2, A);
+    const float n = (float)n_down;
+    float pw, dw;
+    if (P.kappa_ge_one) {
+      const float rc = n * P.inv_kappa;
+      const float den = 1.0f + rc;
+      pw = 1.0f / den;
+      dw = rc / den;
+    } else {
+      const float den = P.kappa + n;
+      pw = P.kappa / den;
+      dw = n / den;
+    }
+    const float2 repaired = make_float2(pw * vprior.x + dw * w2[0], pw * vprior.y + dw * w2[1]);
+    const float2 new_value = n_down > 0 ? repaired : valpha;
+    // _set_node_update (utils.py:53-64)
+    if (present && unresolved) {
+      T.edge_payload[e] = nep;
+      T.edge_alpha[e] = make_float2(e0, e1);
+    }
+    // _categorize_node_and_publish (utils.py:67-124), binary outcomes
+    const bool known = present && !inv && !unresolved;
+    const bool has_legal = __syncthreads_or(present && !inv);
+    const bool any_open = __syncthreads_or(present && !inv && unresolved);
+    const bool has_win = __syncthreads_or(known && eo == 1);
+    const int shortest_win = cta_reduce_min<W>(c, (known && eo == 1) ? ep : INT_MAX);
+    const int longest_loss = cta_reduce_max<W>(c, (known && eo == 0) ? ep : INT_MIN);
+    const bool all_cat = has_legal && !any_open;
+    const int8_t candidate = has_win ? 1 : (all_cat ? 0 : kNoOutcome);
+    const int cdist = has_win ? shortest_win : longest_loss;
+    const bool publish_node = node_outcome == kNoOutcome && candidate != kNoOutcome;
+    int sp = 0, ia = 0;
+    bool has_parent = false, has_incoming = false;
+    if (publish_node) {
+      const int parent = T.parents[ni];
+      has_parent = parent != -1 && T.ok(parent);
+      sp = has_parent ? parent : 0;
+      const int first =
+          cta_reduce_min<W>(c, (present && T.children[T.edge(b, sp, a)] == node) ? a : INT_MAX);
+      has_incoming = first != INT_MAX;
+      ia = has_incoming ? first : 0;
+    }
+    if (a == 0) {
+      T.node_payload[ni] = n_down;
+      T.value_alpha[ni] = new_value;
+      if (publish_node) {
+        const size_t pe = T.edge(b, sp, ia), pn = T.node(b, sp);
+        const bool publish_edge = has_parent && has_incoming && T.edge_outcome[pe] == kNoOutcome;
+        const int new_support = T.node_payload[pn] + 1 + n_down - T.edge_payload[pe];
+        const int8_t aligned = align_cat(candidate, node_tp, T.to_play[pn]);
+        if (publish_edge) T.node_payload[pn] = new_support;
+        T.node_payload[ni] = cdist;
+        T.node_outcome[ni] = candidate;
+        if (publish_edge) {
+          T.edge_outcome[pe] = aligned;
+          T.edge_payload[pe] = cdist + 1;
+        }
+      }
+    }
+    unsafe_n += unsafe;
+    nodes += 1;
+    if (stats) child_gathers += (unsigned long long)cta_reduce_add<W>(c, present && cvis);
+    __syncthreads();
+    const bool up = node != 0;
+    const int parent = T.parents[ni];
+    if (up && !T.ok(parent)) break;
+    node = up ? parent : 0;
+    active = up;
+    leaf_active = false;
+    k = next_key;
+  }
+  if (stats && a == 0) {
+    atomicAdd(stats + 0, nodes);
+    atomicAdd(stats + 1, child_gathers);
+    if (unsafe_n) atomicAdd(stats + 2, unsafe_n);
+  }
+}

@@ -176,14 +176,28 @@ __device__ __forceinline__ DrawKeys draw_keys(sk_key key) {
   return k;
 }
 
-// log Gamma(alpha) variate at flat index idx of a [4, *shape] proposal draw
-// whose proposal axis has stride `stride`.
-__device__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride, float alpha_in) {
+// Per-concentration constants of the Marsaglia-Tsang draw; they depend only
+// on alpha, so a node's Monte Carlo population computes them once.
+struct GammaShape {
+  float alpha, d, c, logd;
+};
+
+__device__ __forceinline__ GammaShape gamma_shape(float alpha_in) {
+  GammaShape g;
   float alpha = alpha_in > SM_TINY ? alpha_in : SM_TINY;
   if (alpha_in != alpha_in) alpha = alpha_in;
   const float shape = alpha < 1.0f ? alpha + 1.0f : alpha;
-  const float d = shape - 0.333333343f;
-  const float c = sm_rsqrtf(9.0f * d);
+  g.alpha = alpha;
+  g.d = shape - 0.333333343f;
+  g.c = sm_rsqrtf(9.0f * g.d);
+  g.logd = sm_logf(g.d);
+  return g;
+}
+
+// log Gamma(alpha) variate at flat index idx of a [4, *shape] proposal draw
+// whose proposal axis has stride `stride`.
+__device__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride, const GammaShape &g) {
+  const float alpha = g.alpha, d = g.d, c = g.c;
   float chosen = 0.0f;
   bool found = false;
   float z0 = 0.0f;
@@ -210,9 +224,13 @@ __device__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride
     fb = fb > floor_ ? fb : floor_;
     chosen = fb * (fb * fb);
   }
-  float lg = sm_logf(d) + sm_logf(chosen);
+  float lg = g.logd + sm_logf(chosen);
   if (alpha < 1.0f) lg = lg + sm_logf(sk_uniform_tiny(k.augment, idx)) / alpha;
   return lg;
+}
+
+__device__ __forceinline__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride, float alpha) {
+  return log_gamma_draw(k, idx, stride, gamma_shape(alpha));
 }
 
 // outcome_utility(softmax([lg0, lg1])), outcomes.py:34-35
@@ -808,6 +826,8 @@ __device__ void store_and_publish(const Tree &T, int b, int n, int lane, const N
   }
   __syncwarp();
 }
+
+#include "lane_cta.cuh"
 
 // ------------------------------------------------------------------------
 // kernels
@@ -1616,6 +1636,8 @@ bool params_ok(const scacchi_update_params *p) {
   return true;
 }
 
+constexpr size_t kCtaSmemLimit = 160 * 1024;
+
 size_t prefix_smem(int half_width) { return (size_t)kWarpsPerBlock * 6 * (2 * half_width + 1) * sizeof(float); }
 
 template <typename K>
@@ -1676,9 +1698,11 @@ int scacchi_simulate(const scacchi_tree *tree, const uint32_t *simulate_key, int
   if (tree->batch == 0) return SCACCHI_OK;
   Tree T = make_tree(tree);
   uint8_t *pe = T.E > 0 ? parent_embedding : nullptr;
-  SCACCHI_DISPATCH(T.A, (simulate_kernel<NS><<<blocks_for(T.B), kThreads, 0, as_stream(stream)>>>(
-                               T, simulate_key, max_depth, parent, action, active, pe,
-                               reinterpret_cast<unsigned long long *>(stats))));
+  SCACCHI_DISPATCH(T.A, {
+    const size_t smem = cta_smem_floats<NS>(1) * sizeof(float);
+    simulate_cta_kernel<NS><<<T.B, 32 * NS, smem, as_stream(stream)>>>(
+        T, simulate_key, max_depth, parent, action, active, pe, reinterpret_cast<unsigned long long *>(stats));
+  });
   return launched();
 }
 
@@ -1708,12 +1732,23 @@ int scacchi_backward(const scacchi_tree *tree, const uint32_t *backward_key, con
   if (tree->batch == 0) return SCACCHI_OK;
   Tree T = make_tree(tree);
   const UpdateParams P = make_params(params);
-  const size_t smem = prefix_smem(P.rule == 1 ? P.prefix.h : 1);
+  const int Q = P.rule == 1 ? 2 * P.prefix.h + 1 : 1;
   SCACCHI_DISPATCH(T.A, {
-    allow_smem(backward_kernel<NS>, smem);
-    backward_kernel<NS><<<blocks_for(T.B), kThreads, smem, as_stream(stream)>>>(
-        T, backward_key, parent, action, active, reinterpret_cast<const float2 *>(step_value), step_to_play, P,
-        reinterpret_cast<unsigned long long *>(stats));
+    const size_t smem = cta_smem_floats<NS>(Q) * sizeof(float);
+    if (smem <= kCtaSmemLimit) {
+      allow_smem(backward_cta_kernel<NS>, smem);
+      backward_cta_kernel<NS><<<T.B, 32 * NS, smem, as_stream(stream)>>>(
+          T, backward_key, parent, action, active, reinterpret_cast<const float2 *>(step_value), step_to_play, P,
+          reinterpret_cast<unsigned long long *>(stats));
+    } else {
+      // very fine grids: the warp-per-lane kernel recomputes instead of
+      // holding [Q][A] matrices in shared memory
+      const size_t wsmem = prefix_smem(P.rule == 1 ? P.prefix.h : 1);
+      allow_smem(backward_kernel<NS>, wsmem);
+      backward_kernel<NS><<<blocks_for(T.B), kThreads, wsmem, as_stream(stream)>>>(
+          T, backward_key, parent, action, active, reinterpret_cast<const float2 *>(step_value), step_to_play, P,
+          reinterpret_cast<unsigned long long *>(stats));
+    }
   });
   return launched();
 }

@@ -132,3 +132,22 @@ def test_search_boundary_targets(cuda):
     assert np.array_equal(targets.prediction.alpha_v.cpu().numpy(), s["value_alpha"])
     assert np.array_equal(targets.metadata.search_action.cpu().numpy(), want.action)
     assert np.array_equal(targets.metadata.q_target_distance.cpu().numpy(), s["q_categorical_distance"])
+
+
+def test_fine_grid_search_uses_warp_kernel_bit_exact(cuda):
+    """half_width 100 (Q = 201) does not fit the per-lane CTA's shared-memory
+    matrices, so backward runs the warp-per-lane kernel; same results."""
+    from oracle import oracle as O
+    from scacchi_b200 import dirichlet_mctx as dm
+    from scacchi_b200 import random as R
+    from scacchi_b200.synthetic import SyntheticGame, SyntheticGameConfig
+
+    B, N = 24, 12
+    game = SyntheticGame(SyntheticGameConfig(seed=9, terminal_prob=0.05))
+    rule = functools.partial(dm.update_posterior_prefix_cdf, kappa=1.0, half_width=100, fallback_policy_samples=4)
+    out = dm.dirichlet_thompson_policy((), R.PRNGKey(2), root=game.root(B), recurrent_fn=game, num_simulations=N,
+                                       posterior_update=rule, max_depth=N, policy_samples=4)
+    want = O.search_synthetic(O.synth_params(seed=9, terminal_prob=0.05), B, O.PRNGKey(2), N,
+                              O.Rule(prefix_cdf=True, kappa=1.0, samples=4, half_width=100), max_depth=N,
+                              policy_samples=4)
+    compare(out, want)
