@@ -266,6 +266,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiling mode: warmup steps + one device-resident step, no JSON line "
+                         "(for ncu captures of the bench workload)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -321,6 +324,12 @@ def main() -> None:
     for _ in range(args.warmup):
         gather(search(state, key))
     torch.cuda.synchronize()
+    if args.profile:
+        gather(search(state, key))
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.destroy_process_group()
+        return
     barrier()
     torch.cuda.synchronize()
     launches0 = _lib.launch_count()

@@ -25,12 +25,16 @@ struct Cta {
   float *lx, *l1mx, *lj, *flp, *joint, *score;  // [Q]
   float *zc;         // [Q] zero counts (exact small integers)
   float *D, *F, *X, *Z;  // [Q][kT]
+  DrawKeys *keys;        // [kKeyChunk] derived keys of a chunk of samples
   int Q;
 };
 
+constexpr int kKeyChunk = 32;
+
 template <int W>
 __host__ __device__ constexpr size_t cta_smem_floats(int Q) {
-  return (size_t)4 * Cta<W>::kT + 16 + 2 * W + 7 * (size_t)Q + 4 * (size_t)Q * Cta<W>::kT;
+  return (size_t)4 * Cta<W>::kT + 16 + 2 * W + 7 * (size_t)Q + 4 * (size_t)Q * Cta<W>::kT +
+         (size_t)kKeyChunk * (sizeof(DrawKeys) / sizeof(float));
 }
 
 template <int W>
@@ -58,6 +62,8 @@ __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
   c.F = p + (size_t)Q * Cta<W>::kT;
   c.X = p + 2 * (size_t)Q * Cta<W>::kT;
   c.Z = p + 3 * (size_t)Q * Cta<W>::kT;
+  p += 4 * (size_t)Q * Cta<W>::kT;
+  c.keys = reinterpret_cast<DrawKeys *>(p);
   c.Q = Q;
   return c;
 }
@@ -196,15 +202,14 @@ __device__ __forceinline__ float cta_max_float(const Cta<W> &c, float v) {
 
 // thompson_sample (action_selection.py:135-143) with one action per thread
 template <int W>
-__device__ int cta_thompson(const Cta<W> &c, sk_key key, const GammaShape &g0, const GammaShape &g1, bool masked,
-                            int8_t cat, bool use_cat, int A, uint64_t lane_base, uint64_t stride) {
+__device__ int cta_thompson(const Cta<W> &c, const DrawKeys &k, const GammaShape &g0, const GammaShape &g1,
+                            bool masked, int8_t cat, bool use_cat, int A, uint64_t lane_base, uint64_t stride) {
   const int a = threadIdx.x;
   float u = -SM_INF;
   if (a < A && !masked) {
     if (use_cat && cat != kNoOutcome) {
       u = cat == 1 ? 1.0f : (cat == 0 ? -1.0f : 0.0f);
     } else {
-      const DrawKeys k = draw_keys(key);
       const uint64_t base = lane_base + (uint64_t)a * 2u;
       const float lg0 = log_gamma_draw(k, base, stride, g0);
       const float lg1 = log_gamma_draw(k, base + 1, stride, g1);
@@ -212,6 +217,16 @@ __device__ int cta_thompson(const Cta<W> &c, sk_key key, const GammaShape &g0, c
     }
   }
   return cta_argmax_by_action<W>(c, u, A);
+}
+
+// the three draw keys of one Thompson sample, derived by one thread
+template <int W>
+__device__ __forceinline__ DrawKeys cta_draw_keys(const Cta<W> &c, sk_key key) {
+  if (threadIdx.x == 0) c.keys[0] = draw_keys(key);
+  __syncthreads();
+  const DrawKeys k = c.keys[0];
+  __syncthreads();
+  return k;
 }
 
 // posterior_best_policy (action_selection.py:146-194), one action per thread
@@ -227,15 +242,23 @@ __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, 
     g1 = gamma_shape(a1);
   }
   if (S == 1) {
-    const int best = cta_thompson<W>(c, key, g0, g1, invalid, cat, use_cat, A, lane_base, stride);
+    const DrawKeys k = cta_draw_keys<W>(c, key);
+    const int best = cta_thompson<W>(c, k, g0, g1, invalid, cat, use_cat, A, lane_base, stride);
     return (present && !invalid && a == best) ? 1.0f : 0.0f;
   }
   const sk_key sample_key = sk_split(key, 0);
   float hits = 0.0f;
-  for (int s = 0; s < S; ++s) {
-    const int best =
-        cta_thompson<W>(c, sk_split(sample_key, (uint64_t)s), g0, g1, invalid, cat, use_cat, A, lane_base, stride);
-    if (a == best) hits = hits + 1.0f;
+  for (int s0 = 0; s0 < S; s0 += kKeyChunk) {
+    // derive each sample's keys once per CTA (threefry split tree)
+    const int n = S - s0 < kKeyChunk ? S - s0 : kKeyChunk;
+    if (a < n) c.keys[a] = draw_keys(sk_split(sample_key, (uint64_t)(s0 + a)));
+    __syncthreads();
+    for (int s = 0; s < n; ++s) {
+      const DrawKeys k = c.keys[s];
+      const int best = cta_thompson<W>(c, k, g0, g1, invalid, cat, use_cat, A, lane_base, stride);
+      if (a == best) hits = hits + 1.0f;
+    }
+    __syncthreads();
   }
   const int legal = __syncthreads_count(present && !invalid);
   float policy = (present && !invalid) ? hits / (float)S : 0.0f;
@@ -462,7 +485,7 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
         g1 = gamma_shape(alpha.y);
       }
     }
-    action = cta_thompson<W>(c, sel_key, g0, g1, masked, kNoOutcome, false, A, 0, stride);
+    action = cta_thompson<W>(c, cta_draw_keys<W>(c, sel_key), g0, g1, masked, kNoOutcome, false, A, 0, stride);
     int child = T.children[T.edge(b, node, action)];
     if (child != -1 && !T.ok(child)) child = -1;
     const bool visited = child != -1;
