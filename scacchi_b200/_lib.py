@@ -91,8 +91,10 @@ def lib() -> C.CDLL:
 
     There is no fallback: without the library the search cannot run.
     """
-    path = _build.LIB
+    path = os.environ.get("SCACCHI_B200_LIB", _build.LIB)
     if not os.path.exists(path):
+        if path != _build.LIB:
+            raise FileNotFoundError(f"SCACCHI_B200_LIB={path} does not exist")
         _build.build()
     handle = C.CDLL(path)
     for name, args in SIGNATURES.items():

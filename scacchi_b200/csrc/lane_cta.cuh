@@ -24,17 +24,22 @@ struct Cta {
   int *pi;           // [W] per-warp argmax indices
   float *lx, *l1mx, *lj, *flp, *joint, *score;  // [Q]
   float *zc;         // [Q] zero counts (exact small integers)
-  float *D, *F, *X, *Z;  // [Q][kT]
-  DrawKeys *keys;        // [kKeyChunk] derived keys of a chunk of samples
+  float *D, *F, *X;   // [Qs][kT]; the Monte Carlo population reuses them for [kKeyChunk][kT] utilities
+  uint8_t *Z;         // [Qs][kT] zero-CDF flags
+  DrawKeys *keys;     // [kKeyChunk] derived keys of a chunk of samples
+  int *best;          // [kKeyChunk] argmax of each sample of a chunk
   int Q;
 };
 
 constexpr int kKeyChunk = 32;
 
+// matrix rows: enough for Q grid points and for a chunk of sample utilities
+__host__ __device__ constexpr int cta_rows(int Q) { return Q > 11 ? Q : 11; }
+
 template <int W>
 __host__ __device__ constexpr size_t cta_smem_floats(int Q) {
-  return (size_t)4 * Cta<W>::kT + 16 + 2 * W + 7 * (size_t)Q + 4 * (size_t)Q * Cta<W>::kT +
-         (size_t)kKeyChunk * (sizeof(DrawKeys) / sizeof(float));
+  return (size_t)4 * Cta<W>::kT + 16 + 2 * W + kKeyChunk + (size_t)kKeyChunk * (sizeof(DrawKeys) / sizeof(float)) +
+         7 * (size_t)Q + 3 * (size_t)cta_rows(Q) * Cta<W>::kT + ((size_t)cta_rows(Q) * Cta<W>::kT + 3) / 4;
 }
 
 template <int W>
@@ -50,6 +55,10 @@ __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
   p += W;
   c.pi = reinterpret_cast<int *>(p);
   p += W;
+  c.best = reinterpret_cast<int *>(p);
+  p += kKeyChunk;
+  c.keys = reinterpret_cast<DrawKeys *>(p);
+  p += kKeyChunk * (sizeof(DrawKeys) / sizeof(float));
   c.lx = p;
   c.l1mx = p + Q;
   c.lj = p + 2 * Q;
@@ -58,12 +67,11 @@ __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
   c.score = p + 5 * Q;
   c.zc = p + 6 * Q;
   p += 7 * Q;
+  const size_t m = (size_t)cta_rows(Q) * Cta<W>::kT;
   c.D = p;
-  c.F = p + (size_t)Q * Cta<W>::kT;
-  c.X = p + 2 * (size_t)Q * Cta<W>::kT;
-  c.Z = p + 3 * (size_t)Q * Cta<W>::kT;
-  p += 4 * (size_t)Q * Cta<W>::kT;
-  c.keys = reinterpret_cast<DrawKeys *>(p);
+  c.F = p + m;
+  c.X = p + 2 * m;
+  c.Z = reinterpret_cast<uint8_t *>(p + 3 * m);
   c.Q = Q;
   return c;
 }
@@ -200,6 +208,9 @@ __device__ __forceinline__ float cta_max_float(const Cta<W> &c, float v) {
   return m;
 }
 
+__device__ __forceinline__ float draw_utility(const DrawKeys &k, const GammaShape &g0, const GammaShape &g1,
+                                              uint64_t base, uint64_t stride);
+
 // thompson_sample (action_selection.py:135-143) with one action per thread
 template <int W>
 __device__ int cta_thompson(const Cta<W> &c, const DrawKeys &k, const GammaShape &g0, const GammaShape &g1,
@@ -210,10 +221,7 @@ __device__ int cta_thompson(const Cta<W> &c, const DrawKeys &k, const GammaShape
     if (use_cat && cat != kNoOutcome) {
       u = cat == 1 ? 1.0f : (cat == 0 ? -1.0f : 0.0f);
     } else {
-      const uint64_t base = lane_base + (uint64_t)a * 2u;
-      const float lg0 = log_gamma_draw(k, base, stride, g0);
-      const float lg1 = log_gamma_draw(k, base + 1, stride, g1);
-      u = binary_utility(lg0, lg1);
+      u = draw_utility(k, g0, g1, lane_base + (uint64_t)a * 2u, stride);
     }
   }
   return cta_argmax_by_action<W>(c, u, A);
@@ -229,39 +237,68 @@ __device__ __forceinline__ DrawKeys cta_draw_keys(const Cta<W> &c, sk_key key) {
   return k;
 }
 
-// posterior_best_policy (action_selection.py:146-194), one action per thread
+// exact utility of a categorical edge (outcomes.py:38-43)
+__device__ __forceinline__ float categorical_utility(int8_t cat) {
+  return cat == 1 ? 1.0f : (cat == 0 ? -1.0f : 0.0f);
+}
+
+// utility of one Thompson draw of this thread's action
+__device__ __forceinline__ float draw_utility(const DrawKeys &k, const GammaShape &g0, const GammaShape &g1,
+                                              uint64_t base, uint64_t stride) {
+  const float lg0 = log_gamma_draw(k, base, stride, g0);
+  const float lg1 = log_gamma_draw(k, base + 1, stride, g1);
+  return binary_utility(lg0, lg1);
+}
+
+// posterior_best_policy (action_selection.py:146-194), one action per thread.
+// Each thread first draws its action's utility for every sample of a chunk
+// (independent work, no barrier), then warps take one sample's argmax each.
 template <int W>
 __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, bool invalid, int8_t cat,
                                bool use_cat, int S, int A, int b, int B) {
-  const int a = threadIdx.x;
+  constexpr int T = Cta<W>::kT;
+  const int a = threadIdx.x, lane = a % kWarp, warp = a / kWarp;
   const bool present = a < A;
-  const uint64_t lane_base = (uint64_t)b * A * 2u, stride = (uint64_t)B * A * 2u;
+  const bool exact = present && !invalid && use_cat && cat != kNoOutcome;
+  const bool sampled = present && !invalid && !exact;
+  const uint64_t base = (uint64_t)b * A * 2u + (uint64_t)a * 2u, stride = (uint64_t)B * A * 2u;
   GammaShape g0 = gamma_shape(1.0f), g1 = g0;
-  if (present && !invalid && !(use_cat && cat != kNoOutcome)) {
+  if (sampled) {
     g0 = gamma_shape(a0);
     g1 = gamma_shape(a1);
   }
-  if (S == 1) {
-    const DrawKeys k = cta_draw_keys<W>(c, key);
-    const int best = cta_thompson<W>(c, k, g0, g1, invalid, cat, use_cat, A, lane_base, stride);
-    return (present && !invalid && a == best) ? 1.0f : 0.0f;
-  }
+  const float fixed = exact ? categorical_utility(cat) : -SM_INF;
+  // one sample draws with `key` itself; more samples split(split(key)[0], S)
   const sk_key sample_key = sk_split(key, 0);
-  float hits = 0.0f;
+  int hits = 0;
+  float *U = c.D;  // [kKeyChunk][T]
   for (int s0 = 0; s0 < S; s0 += kKeyChunk) {
-    // derive each sample's keys once per CTA (threefry split tree)
     const int n = S - s0 < kKeyChunk ? S - s0 : kKeyChunk;
-    if (a < n) c.keys[a] = draw_keys(sk_split(sample_key, (uint64_t)(s0 + a)));
+    if (a < n) c.keys[a] = draw_keys(S == 1 ? key : sk_split(sample_key, (uint64_t)(s0 + a)));
     __syncthreads();
-    for (int s = 0; s < n; ++s) {
-      const DrawKeys k = c.keys[s];
-      const int best = cta_thompson<W>(c, k, g0, g1, invalid, cat, use_cat, A, lane_base, stride);
-      if (a == best) hits = hits + 1.0f;
+    for (int s = 0; s < n; ++s) U[s * T + a] = sampled ? draw_utility(c.keys[s], g0, g1, base, stride) : fixed;
+    __syncthreads();
+    for (int s = warp; s < n; s += W) {
+      float bv = -SM_INF;
+      int bi = INT_MAX;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        const int aa = lane + kWarp * j;
+        if (aa < A && beats(U[s * T + aa], aa, bv, bi)) {
+          bv = U[s * T + aa];
+          bi = aa;
+        }
+      }
+      const int w = warp_argmax(bv, bi);
+      if (lane == 0) c.best[s] = w;
     }
     __syncthreads();
+    for (int s = 0; s < n; ++s) hits += c.best[s] == a;
+    __syncthreads();
   }
+  if (S == 1) return (present && !invalid && hits) ? 1.0f : 0.0f;
   const int legal = __syncthreads_count(present && !invalid);
-  float policy = (present && !invalid) ? hits / (float)S : 0.0f;
+  float policy = (present && !invalid) ? (float)hits / (float)S : 0.0f;
   const float total = cta_sum<W>(c, policy, A);
   const float denom = total > 1.0f ? total : 1.0f;
   const float lc = (float)(legal > 1 ? legal : 1);
@@ -361,13 +398,16 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
     const float m = f < 0.0f ? f : 0.0f;
     c.F[k * T + a] = f;
     c.X[k * T + a] = unres ? (pos ? m : -SM_INF) : 0.0f;
-    c.Z[k * T + a] = (unres && !pos) ? 1.0f : 0.0f;
+    c.Z[k * T + a] = (unres && !pos) ? 1 : 0;
   }
   __syncthreads();
   for (int k = warp; k < Q; k += W) {
     const float flp = column_sum<W>(c.F + k * T, A, lane);
     const float lsum = column_sum<W>(c.X + k * T, A, lane);
-    const float z = column_sum<W>(c.Z + k * T, A, lane);
+    int zl = 0;
+#pragma unroll
+    for (int j = 0; j < W; ++j) zl += lane + kWarp * j < A ? c.Z[k * T + lane + kWarp * j] : 0;
+    const float z = (float)__reduce_add_sync(kFull, zl);
     if (lane == 0) {
       c.flp[k] = flp;
       c.joint[k] = sm_expf(lsum);
@@ -516,8 +556,12 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
 }
 
 // backward (search.py:146-171) with the built-in rules, one CTA per lane
+#ifndef SCACCHI_BWD_MIN_BLOCKS
+#define SCACCHI_BWD_MIN_BLOCKS 8
+#endif
+
 template <int W>
-__global__ void __launch_bounds__(32 * W) backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent,
+__global__ void __launch_bounds__(32 * W, SCACCHI_BWD_MIN_BLOCKS) backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent,
                                                               const int32_t *sim_action, const uint8_t *sim_active,
                                                               const float2 *step_value, const int32_t *step_tp,
                                                               UpdateParams P, unsigned long long *stats) {

@@ -196,7 +196,14 @@ __device__ __forceinline__ GammaShape gamma_shape(float alpha_in) {
 
 // log Gamma(alpha) variate at flat index idx of a [4, *shape] proposal draw
 // whose proposal axis has stride `stride`.
-__device__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride, const GammaShape &g) {
+#ifdef SCACCHI_NOINLINE_DRAW
+#define SCACCHI_DRAW_INLINE __noinline__
+#else
+#define SCACCHI_DRAW_INLINE
+#endif
+
+__device__ SCACCHI_DRAW_INLINE float log_gamma_draw(const DrawKeys k, uint64_t idx, uint64_t stride,
+                                                    const GammaShape g) {
   const float alpha = g.alpha, d = g.d, c = g.c;
   float chosen = 0.0f;
   bool found = false;
