@@ -241,6 +241,70 @@ int scacchi_search_synthetic(const scacchi_tree *tree, const scacchi_synthetic_p
                              const scacchi_update_params *params, void *workspace, uint64_t *stats,
                              void *stream);
 
+/* ---- leaf evaluation: AZDirichletNet (network.py:338-524) -------------- */
+
+/* Inference weights of the 9x9 resnet_v2 AZDirichletNet with binary
+ * outcomes, BatchNorm in inference form (running statistics):
+ *   stem_w      float32 [9 taps (ky*3+kx)][in_planes][128], stem_b [128]
+ *   bn_scale/shift float32 [num_blocks + 1][128]: BN1 of every block, then
+ *               the trunk's final BN, as y = x * scale + shift
+ *   conv_w      16-bit [2 * num_blocks][9 taps][128 out][128 in] (bf16, or
+ *               fp16 when fp16 = 1); the BN after
+ *               each block's first conv is folded into that conv's weights
+ *               and bias; conv_b float32 [2 * num_blocks][128]
+ *   head_w      float32 [6][128], head_b [6]: 1x1 convs of the policy (2),
+ *               value (1), Q-mean (2) and Q-concentration (1) heads with
+ *               their BNs folded
+ *   dense layers as [in][out] row-major with flax's flatten order
+ *               (y, x, channel). */
+typedef struct {
+  int32_t num_blocks, channels, height, width, in_planes, num_actions;
+  int32_t fp16;  /* 16-bit operand and activation type: 0 bf16, 1 fp16 */
+  const float *stem_w, *stem_b;
+  const float *bn_scale, *bn_shift;
+  const uint16_t *conv_w;
+  const float *conv_b;
+  const float *head_w, *head_b;
+  const float *policy_w, *policy_b;          /* [162][A], [A] */
+  const float *value_w1, *value_b1;          /* [81][128], [128] */
+  const float *value_mean_w, *value_mean_b;  /* [128][2], [2] */
+  const float *value_conc_w, *value_conc_b;  /* [128], [1] */
+  const float *qdir_w1, *qdir_b1;            /* [162][128], [128] */
+  const float *qdir_w2, *qdir_b2;            /* [128][2A], [2A] */
+  const float *qconc_w1, *qconc_b1;          /* [81][128], [128] */
+  const float *qconc_w2, *qconc_b2;          /* [128][A], [A] */
+} scacchi_tower_weights;
+
+/* Rows of one padded activation matrix for `boards` boards (100 rows per
+ * board, rounded up to the 128-row tile) and the workspace the forward
+ * pass needs (three bf16 [rows, 128] activations + head features). */
+uint64_t scacchi_tower_rows(int32_t boards);
+size_t scacchi_tower_workspace_bytes(int32_t boards);
+
+/* AZDirichletNet.__call__(obs, train=False): obs float32 [B, 9, 9, planes]
+ * -> logits [B, A], log alpha_v [B, 2], log alpha_q [B, A, 2] (log
+ * concentration + log softmax of the mean logits) and the alphas
+ * themselves.  bf16 tensor-core convolutions, fp32 accumulation. */
+int scacchi_tower_forward(const scacchi_tower_weights *weights, const float *obs, int32_t boards, void *workspace,
+                          float *logits, float *log_alpha_v, float *log_alpha_q, float *alpha_v, float *alpha_q,
+                          void *stream);
+
+/* One padded-layout conv3x3 128->128 (tcgen05 implicit GEMM on 16-bit
+ * operands, bf16 or fp16, fp32 accumulation) with its
+ * fused epilogue: mode 0 out0 = relu(conv + bias); mode 1 out0 = x' =
+ * conv + bias + residual, out1 = relu(x' * bn_scale + bn_shift); mode 2 as
+ * mode 1 then the six 1x1 head channels relu(out1 . head_w + head_b) into
+ * head_out float32 [rows, 8].  Padding rows are written as zero. */
+int scacchi_conv3x3(const void *input, const void *weights, const float *bias, int32_t mode, int32_t boards,
+                    int32_t fp16, const float *bn_scale, const float *bn_shift, const void *residual,
+                    const float *head_w, const float *head_b, void *out0, void *out1, float *head_out,
+                    void *stream);
+
+/* Sticky tower error flags (bit 0: a bounded wait timed out); reading
+ * synchronises and clears.  Launch counter of the tower kernels. */
+int scacchi_tower_error(uint32_t *flags);
+uint64_t scacchi_tower_launch_count(void);
+
 /* ---- host-side jax.random key helpers (no device work) ---------------- */
 
 /* search.py:207-209 key chain: for i < num_simulations,

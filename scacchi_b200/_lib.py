@@ -49,6 +49,15 @@ class Context(C.Structure):
         "child_to_play")]
 
 
+class TowerWeights(C.Structure):
+    POINTERS = ("stem_w", "stem_b", "bn_scale", "bn_shift", "conv_w", "conv_b", "head_w", "head_b", "policy_w",
+                "policy_b", "value_w1", "value_b1", "value_mean_w", "value_mean_b", "value_conc_w", "value_conc_b",
+                "qdir_w1", "qdir_b1", "qdir_w2", "qdir_b2", "qconc_w1", "qconc_b1", "qconc_w2", "qconc_b2")
+    _fields_ = [(n, C.c_int32) for n in ("num_blocks", "channels", "height", "width", "in_planes", "num_actions",
+                                         "fp16")] + [
+        (n, C.c_void_p) for n in POINTERS]
+
+
 P = C.c_void_p
 I32 = C.c_int32
 F32 = C.c_float
@@ -75,10 +84,18 @@ SIGNATURES = {
     "scacchi_key_schedule": [C.c_uint32, C.c_uint32, I32, P],
     "scacchi_split_host": [C.c_uint32, C.c_uint32, I32, P],
     "scacchi_fold_in_host": [C.c_uint32, C.c_uint32, C.c_uint32, P],
+    "scacchi_tower_rows": [I32],
+    "scacchi_tower_workspace_bytes": [I32],
+    "scacchi_tower_forward": [C.POINTER(TowerWeights), P, I32, P, P, P, P, P, P, P],
+    "scacchi_conv3x3": [P, P, P, I32, I32, I32, P, P, P, P, P, P, P, P, P],
+    "scacchi_tower_error": [P],
+    "scacchi_tower_launch_count": [],
     "scacchi_device_error": [P],
     "scacchi_launch_count": [],
 }
-RESTYPES = {"scacchi_search_workspace_bytes": C.c_size_t, "scacchi_launch_count": C.c_uint64}
+RESTYPES = {"scacchi_search_workspace_bytes": C.c_size_t, "scacchi_launch_count": C.c_uint64,
+            "scacchi_tower_rows": C.c_uint64, "scacchi_tower_workspace_bytes": C.c_size_t,
+            "scacchi_tower_launch_count": C.c_uint64}
 
 
 class ScacchiError(RuntimeError):
@@ -119,4 +136,11 @@ def device_error() -> int:
 
 
 def launch_count() -> int:
-    return int(lib().scacchi_launch_count())
+    """Kernels this library launched since load (search + network)."""
+    return int(lib().scacchi_launch_count()) + int(lib().scacchi_tower_launch_count())
+
+
+def tower_error() -> int:
+    flags = C.c_uint32(0)
+    check(lib().scacchi_tower_error(C.byref(flags)), "scacchi_tower_error")
+    return int(flags.value)
