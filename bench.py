@@ -198,6 +198,80 @@ def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dic
     }
 
 
+TOWER_BOARDS = 16384
+CONV_FLOP_PER_BOARD = 2 * 81 * 128 * 128 * 9          # one 3x3 128->128 conv
+TOWER_FLOP_PER_BOARD = 12 * CONV_FLOP_PER_BOARD + 2 * 81 * 4 * 128 * 9 + 2 * (
+    81 * 128 * 6 + 162 * 82 + 81 * 128 + 128 * 3 + 162 * 128 + 128 * 164 + 81 * 128 + 128 * 82)
+
+
+def read_tensor_peak() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
+    """Residual tower alone: 16384 boards of {0,1} planes (density 0.4),
+    He-normal weights on every layer (seed 0), 16-bit operands with fp32
+    accumulation.  Inputs (12.7 MB of planes) are resident; the activations
+    the tower streams (3 x 420 MB) exceed L2."""
+    import torch
+
+    from oracle.network_ref import observations  # input generator only
+    from scacchi_b200.network import AZDirichletNet, init_params
+
+    net = AZDirichletNet(init_params(0), fp16=fp16)
+    obs = torch.from_numpy(observations(TOWER_BOARDS, seed=0)).cuda()
+    for _ in range(warmup):
+        net(obs)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        net(obs)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # the conv kernel alone (one launch of the 12), timed on its stream
+    import ctypes as C
+    from scacchi_b200 import _lib
+    from scacchi_b200.dirichlet_mctx.tree import ptr
+
+    rows = int(_lib.lib().scacchi_tower_rows(TOWER_BOARDS))
+    act = torch.zeros((rows, 128), dtype=torch.float16 if fp16 else torch.bfloat16, device="cuda")
+    out = torch.empty_like(act)
+    w = net.weights.tensors["conv_w"][0]
+    b = net.weights.tensors["conv_b"][0]
+    sh = C.c_void_p(stream.cuda_stream)
+    call = lambda: _lib.lib().scacchi_conv3x3(ptr(act), ptr(w), ptr(b), 0, TOWER_BOARDS, int(fp16), None, None, None,
+                                              None, None, ptr(out), None, None, sh)
+    for _ in range(3):
+        call()
+    e0.record(stream)
+    for _ in range(10):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    conv_ms = e0.elapsed_time(e1) / 10
+    peak, kind = read_tensor_peak()
+    conv_tflops = CONV_FLOP_PER_BOARD * TOWER_BOARDS / (conv_ms / 1e3) / 1e12
+    return {
+        "boards": TOWER_BOARDS, "dtype": "fp16" if fp16 else "bf16", "ms_per_forward": round(ms, 4),
+        "evals_per_s": round(TOWER_BOARDS / (ms / 1e3), 1),
+        "tflops": round(TOWER_FLOP_PER_BOARD * TOWER_BOARDS / (ms / 1e3) / 1e12, 2),
+        "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": round(conv_tflops, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(conv_tflops / peak, 4), "traffic": None, "peak_source": kind,
+                     "avg_launch_ms": round(conv_ms, 4),
+                     "algorithmic_flop_per_launch": CONV_FLOP_PER_BOARD * TOWER_BOARDS,
+                     "note": "algorithmic FLOPs count the 81 board cells; the kernel also multiplies the 19 "
+                             "padding rows of each 100-row board (x1.23)"},
+    }
+
+
 def cpu_baseline(lanes: int = 48) -> dict:
     """The C oracle (a restatement of the reference's JAX path, which cannot
     be installed here) on a bounded sample: lanes [0, lanes) of the same
@@ -266,6 +340,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="search", choices=["search", "tower"],
+                    help="search: the isolated search kernels (default); tower: the residual tower alone")
+    ap.add_argument("--fp16", action="store_true", help="tower: fp16 operands instead of bf16")
     ap.add_argument("--profile", action="store_true",
                     help="profiling mode: warmup steps + one device-resident step, no JSON line "
                          "(for ncu captures of the bench workload)")
@@ -285,6 +362,27 @@ def main() -> None:
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.workload == "tower":
+        if args.profile:
+            from oracle.network_ref import observations
+            from scacchi_b200.network import AZDirichletNet, init_params
+
+            net = AZDirichletNet(init_params(0), fp16=args.fp16)
+            obs = torch.from_numpy(observations(TOWER_BOARDS, seed=0)).cuda()
+            for _ in range(args.warmup + 1):
+                net(obs)
+            torch.cuda.synchronize()
+            return
+        if rank == 0:
+            t = tower_bench(args.steps, args.warmup, args.fp16)
+            print(json.dumps({"metric": "residual tower leaf evals/s (16384 boards)", "value": t["evals_per_s"],
+                              "unit": "evals/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                              "ms_per_step": t["ms_per_forward"], "higher_is_better": True, "scaling": "weak",
+                              "vs_baseline": None, "dtype": t["dtype"], "data": "synthetic",
+                              "config": {"workload": "residual tower alone: 6x128 ResNet, 9x9x4 {0,1} planes "
+                                                     "(density 0.4), He-normal weights seed 0", "boards": TOWER_BOARDS},
+                              "tflops": t["tflops"], "roofline": t["roofline"]}), flush=True)
+        return
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
 
@@ -405,6 +503,8 @@ def main() -> None:
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": int(launches), "roofline": roof,
         }
+        if world == 1:
+            line["tower"] = tower_bench(5, 3)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

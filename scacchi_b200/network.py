@@ -83,7 +83,7 @@ class AZDirichletParams:
 
 def init_params(seed: int = 0, *, num_actions: int = 82, in_planes: int = 4, channels: int = 128,
                 num_blocks: int = 6, he_all_layers: bool = True, random_batchnorm: bool = False,
-                initial_concentration: float = 3.1) -> AZDirichletParams:
+                initial_concentration: float = 3.1, block_gain: float = 1.0) -> AZDirichletParams:
     """He-normal weights (std sqrt(2 / fan_in)), zero biases.
 
     ``he_all_layers=False`` reproduces the reference's random init, whose
@@ -91,7 +91,8 @@ def init_params(seed: int = 0, *, num_actions: int = 82, in_planes: int = 4, cha
     zero-initialised with the concentration biases at log(c0)
     (network.py:395-458): constant outputs.  ``random_batchnorm`` draws
     non-trivial BatchNorm statistics (for folding tests); otherwise BatchNorm
-    is at its init (scale 1, bias 0, mean 0, var 1)."""
+    is at its init (scale 1, bias 0, mean 0, var 1).  ``block_gain`` scales
+    the residual blocks' conv weights (1: He-normal)."""
     rng = np.random.default_rng(seed)
     f32 = np.float32
 
@@ -116,8 +117,8 @@ def init_params(seed: int = 0, *, num_actions: int = 82, in_planes: int = 4, cha
     conc0 = math.log(initial_concentration)
     blocks = []
     for _ in range(num_blocks):
-        blocks.append(dict(bn1=bn(Ch), conv1_w=he((3, 3, Ch, Ch), 9 * Ch), conv1_b=zeros(Ch), bn2=bn(Ch),
-                           conv2_w=he((3, 3, Ch, Ch), 9 * Ch), conv2_b=zeros(Ch)))
+        blocks.append(dict(bn1=bn(Ch), conv1_w=block_gain * he((3, 3, Ch, Ch), 9 * Ch), conv1_b=zeros(Ch),
+                           bn2=bn(Ch), conv2_w=block_gain * he((3, 3, Ch, Ch), 9 * Ch), conv2_b=zeros(Ch)))
     pw, pb = head((162, A), 162)
     vdw, vdb = head((Ch, 2), Ch)
     vcw, vcb = head((Ch, 1), Ch, conc0)

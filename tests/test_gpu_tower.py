@@ -113,18 +113,23 @@ def _tower_outputs(params, obs, fp16):
 
 @pytest.mark.parametrize("fp16", [False, True], ids=["bf16", "fp16"])
 def test_tower_matches_rounding_emulation(cuda, fp16):
-    """Kernel arithmetic: same rounding points as the emulation, differences
-    only from fp32 summation order (an occasional 16-bit rounding flip)."""
+    """Kernel arithmetic against the emulation of its own rounding points.
+
+    Summation order differs (tensor cores vs torch), so a value sitting on a
+    16-bit rounding boundary can round the other way, and a He-normal stack
+    amplifies such flips layer by layer.  With block gain 0.5 the network
+    does not amplify and the comparison is tight; the measured deviations on
+    the amplifying workload are covered by the fp32 test below."""
     from oracle import network_ref as R
     from scacchi_b200 import _lib
     from scacchi_b200.network import init_params
 
-    params = init_params(0, random_batchnorm=True)
+    params = init_params(0, random_batchnorm=True, block_gain=0.5)
     obs = R.observations(192, seed=1)
     got = _tower_outputs(params, obs, fp16)
     want = R.forward(params, obs, emulate_bf16=True, fp16=fp16)
     assert _lib.tower_error() == 0
-    tol = 1e-2 if fp16 else 6e-2
+    tol = 6e-3 if fp16 else 4e-2
     for g, w, name in zip(got[:3], want, ("logits", "log_alpha_v", "log_alpha_q")):
         err = np.abs(g - w).max()
         assert err < tol, f"{name}: max abs {err}"
@@ -150,6 +155,7 @@ def test_tower_against_fp32_reference(cuda):
     agree16 = (f16[0].argmax(1) == ref[0].argmax(1)).mean()
     agree_b = (b16[0].argmax(1) == ref[0].argmax(1)).mean()
     print(f"fp16 max abs logits/lav/laq {err16} argmax {agree16}; bf16 {err_b} argmax {agree_b}")
-    assert err16[0] < 3e-2 and err16[1] < 3e-2 and err16[2] < 6e-2
+    # measured on B200: fp16 0.012 / 0.017 / 0.023, bf16 0.09 / 0.17 / 0.22
+    assert err16[0] < 2e-2 and err16[1] < 2.5e-2 and err16[2] < 3.5e-2
     assert agree16 >= 0.995
     assert err_b[0] < 0.3 and err_b[2] < 0.6 and agree_b >= 0.95
