@@ -67,7 +67,7 @@ typedef struct {
   int32_t rule;              /* 0: update_posterior (Monte Carlo), 1: update_posterior_prefix_cdf */
   int32_t kappa_ge_one;      /* kappa >= 1, decided in double precision */
   float inv_kappa;           /* float32(1 / kappa) */
-  float kappa;               /* float32(kappa) */
+  float kappa;               /* float32(kappa), read only when kappa < 1 */
   int32_t samples;           /* policy_samples (rule 0) / fallback_policy_samples (rule 1) */
   int32_t half_width;        /* Q = 2 * half_width + 1 grid points */
   float tail_scale;

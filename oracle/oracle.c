@@ -673,7 +673,7 @@ typedef struct {
  * posterior_updates.py:66-367, for lane b of B. */
 static void posterior_update_lane(sk_key update_key, const or_context *c, int A,
                                   const or_update_params *u, int b, int B, or_update *out) {
-  float eff[2 * MAX_ACTIONS], cache[2 * MAX_ACTIONS];
+  float eff[2 * MAX_ACTIONS] = {0}, cache[2 * MAX_ACTIONS] = {0};
   int32_t count_delta = 0;
   int leaf_action = c->leaf_action < 0 ? c->leaf_action + A : c->leaf_action;
   float direct[2];
@@ -1024,7 +1024,7 @@ void or_normal(uint32_t k0, uint32_t k1, uint64_t n, float *out) {
   for (uint64_t i = 0; i < n; ++i) out[i] = sk_normal(k, i);
 }
 
-/* scalar math, vectorised for tests/test_smath.py */
+/* scalar math, vectorised for tests/test_oracle_pins.py */
 void or_math(int fn, const float *x, const float *y, int n, float *out) {
   for (int i = 0; i < n; ++i) {
     float v = x[i];
@@ -1274,7 +1274,7 @@ static void normalize_on_support(const float *policy, const uint8_t *support, in
     if (scaled[a] > smax) smax = scaled[a];
   }
   if (s_nan) smax = SM_NAN;
-  float e[MAX_ACTIONS];
+  float e[MAX_ACTIONS] = {0};
   for (int a = 0; a < A; ++a) e[a] = sm_expf(scaled[a] - smax);
   float total = warp_order_sum(e, A);
   float den = (float)(count > 1 ? count : 1);

@@ -248,7 +248,7 @@ class Rule:
     def params(self) -> UpdateParams:
         return UpdateParams(
             1 if self.prefix_cdf else 0, 1 if self.kappa >= 1.0 else 0,
-            float(np.float32(1.0 / self.kappa)), float(np.float32(self.kappa)), int(self.samples),
+            float(np.float32(1.0 / self.kappa)), float(np.float32(min(self.kappa, 1.0))), int(self.samples),
             prefix_params(self.half_width, self.tail_scale, self.min_half_range, self.max_half_range),
             float(np.float32(self.density_tol)))
 

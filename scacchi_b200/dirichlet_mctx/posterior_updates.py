@@ -37,7 +37,7 @@ def _params(rule: int, kappa: float, samples: int, half_width: int = 10, tail_sc
             min_half_range: float = 6.0, max_half_range: float = 11.0,
             density_tol: float = DEFAULT_PREFIX_DENSITY_LOG_INTEGRAL_TOLERANCE) -> _lib.UpdateParams:
     return _lib.UpdateParams(
-        rule, 1 if kappa >= 1.0 else 0, float(np.float32(1.0 / kappa)), float(np.float32(kappa)), int(samples),
+        rule, 1 if kappa >= 1.0 else 0, float(np.float32(1.0 / kappa)), float(np.float32(min(kappa, 1.0))), int(samples),
         int(half_width), float(tail_scale), float(min_half_range), float(max_half_range), float(density_tol))
 
 
