@@ -272,7 +272,7 @@ def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
     }
 
 
-def cpu_baseline(lanes: int = 48) -> dict:
+def cpu_baseline(lanes: int = 384) -> dict:
     """The C oracle (a restatement of the reference's JAX path, which cannot
     be installed here) on a bounded sample: lanes [0, lanes) of the same
     4096-lane workload, one host thread."""
@@ -388,24 +388,21 @@ def main() -> None:
 
     from scacchi_b200 import _lib
     from scacchi_b200 import random as R
+    from scacchi_b200.distributed import LaneSharding, gather_targets
     from scacchi_b200.play_search import make_search
     from scacchi_b200.synthetic import SyntheticGame, SyntheticGameConfig
 
     game = SyntheticGame(SyntheticGameConfig(seed=rank, num_actions=ACTIONS), device=dev)
     cfg = search_config()
     search = make_search(game, game.evaluator, cfg)
-    key = R.split(R.PRNGKey(0), world)[rank]  # play.py:231,243: per-device keys
+    sharding = LaneSharding(world, rank)
+    key = sharding.device_key(R.PRNGKey(0))
     state = game.init(LANES)
     torch.cuda.synchronize()
 
     def gather(targets):
-        if world > 1:
-            pol = targets.prediction.policy.contiguous()
-            out = torch.empty((world * LANES, ACTIONS), dtype=pol.dtype, device=dev)
-            dist.all_gather_into_tensor(out, pol)
-            act = targets.metadata.search_action.contiguous()
-            acts = torch.empty((world * LANES,), dtype=act.dtype, device=dev)
-            dist.all_gather_into_tensor(acts, act)
+        # the step's only collective: root targets of every rank, lane order
+        return gather_targets(targets, sharding)
 
     def barrier():
         if world > 1:
