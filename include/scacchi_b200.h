@@ -40,6 +40,7 @@ extern "C" {
 #define SCACCHI_OK 0
 #define SCACCHI_EINVAL 1
 #define SCACCHI_ECUDA 2
+#define SCACCHI_ETOOLARGE 3 /* larger than a fixed library-owned buffer */
 
 typedef struct {
   int32_t batch;
@@ -240,6 +241,30 @@ int scacchi_search_synthetic(const scacchi_tree *tree, const scacchi_synthetic_p
                              const uint32_t *keys, int32_t num_simulations, int32_t max_depth,
                              const scacchi_update_params *params, void *workspace, uint64_t *stats,
                              void *stream);
+
+/* No counterpart in the reference.  scacchi_search_synthetic for callers
+ * that cannot allocate device memory at call time (an XLA FFI handler,
+ * whose allocator owns the device's memory and offers scratch only as
+ * declared buffers; a server that pins all of HBM to a pool at start-up).
+ * Instead of a caller workspace it uses a scratch array compiled into the
+ * library: SCACCHI_STATIC_SCRATCH_BYTES per device, held by every GPU that
+ * loads the library until the process exits.  The caller still passes the
+ * tree, keys and stats.  It calls no cudaMalloc, cudaFree or allocating
+ * library routine.
+ *   - Sizes whose workspace (scacchi_search_workspace_bytes) exceeds the
+ *     array return SCACCHI_ETOOLARGE; nothing is launched.  At 82 actions
+ *     and 16-byte states the limit is 5,294 lanes.
+ *   - The first call on a device resolves the array's device address with
+ *     that device current (cudaGetSymbolAddress); make that first call
+ *     before any stream capture on the device.
+ *   - All calls on a device share the one array, which keeps the last
+ *     call's contents.  Calls whose work overlaps on the GPU (different
+ *     streams, or different host threads without ordering) race on it and
+ *     corrupt each other's results: order them on one stream. */
+#define SCACCHI_STATIC_SCRATCH_BYTES (4u << 20)
+int scacchi_search_synthetic_static(const scacchi_tree *tree, const scacchi_synthetic_params *env,
+                                    const uint32_t *keys, int32_t num_simulations, int32_t max_depth,
+                                    const scacchi_update_params *params, uint64_t *stats, void *stream);
 
 /* ---- leaf evaluation: AZDirichletNet (network.py:338-524) -------------- */
 

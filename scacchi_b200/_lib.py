@@ -9,6 +9,7 @@ import os
 from . import _build
 
 OK, EINVAL, ECUDA = 0, 1, 2
+ETOOLARGE = 3  # scacchi_search_synthetic_static: batch beyond the library-owned scratch
 
 
 class ScacchiTree(C.Structure):
@@ -81,6 +82,8 @@ SIGNATURES = {
     "scacchi_search_workspace_bytes": [I32, I32, I32],
     "scacchi_search_synthetic": [TREE, C.POINTER(SyntheticParams), P, I32, I32, C.POINTER(UpdateParams), P, P,
                                  P],
+    "scacchi_search_synthetic_static": [TREE, C.POINTER(SyntheticParams), P, I32, I32, C.POINTER(UpdateParams),
+                                        P, P],
     "scacchi_key_schedule": [C.c_uint32, C.c_uint32, I32, P],
     "scacchi_split_host": [C.c_uint32, C.c_uint32, I32, P],
     "scacchi_fold_in_host": [C.c_uint32, C.c_uint32, C.c_uint32, P],

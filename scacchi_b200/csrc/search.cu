@@ -2018,3 +2018,58 @@ int scacchi_fold_in_host(uint32_t k0, uint32_t k1, uint32_t data, uint32_t *out)
 }
 
 }  // extern "C"
+
+// ==========================================================================
+// Synthetic-game search with library-owned scratch (no allocation per call)
+// ==========================================================================
+//
+// Some callers cannot allocate device memory at call time.  The main one is
+// an XLA FFI handler: it runs inside XLA, whose allocator has usually
+// reserved most of the device's memory up front and hands out scratch only
+// as buffers declared in the call's signature, so a cudaMalloc there can
+// fail, or synchronise the device in the middle of XLA's stream ordering.
+// Serving processes that pin every byte of HBM to a pool at start-up are in
+// the same position.  For them this entry point takes its per-simulation
+// buffers from one fixed array compiled into the library instead of a
+// caller workspace.
+//
+// The array is SCACCHI_STATIC_SCRATCH_BYTES (4 MiB) per device.  Every GPU
+// on which the library's search module is loaded holds it until the
+// process exits, whether or not this entry point is used.
+
+static __device__ __align__(256) uint8_t g_search_scratch[SCACCHI_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxScratchDevices = 64;
+// Device address of g_search_scratch per device, resolved on first use.
+std::atomic<void *> g_scratch_addr[kMaxScratchDevices];
+
+}  // namespace
+
+extern "C" {
+
+int scacchi_search_synthetic_static(const scacchi_tree *tree, const scacchi_synthetic_params *env,
+                                    const uint32_t *keys, int32_t num_simulations, int32_t max_depth,
+                                    const scacchi_update_params *params, uint64_t *stats, void *stream) {
+  if (!tree || tree->batch < 0 || tree->num_actions < 1) return SCACCHI_EINVAL;
+  const size_t need = scacchi_search_workspace_bytes(tree->batch, tree->num_actions, tree->emb_bytes);
+  if (need > (size_t)SCACCHI_STATIC_SCRATCH_BYTES) return SCACCHI_ETOOLARGE;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SCACCHI_ECUDA;
+  if (dev < 0 || dev >= kMaxScratchDevices) return SCACCHI_ECUDA;
+  void *scratch = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!scratch) {
+    // Set-up, once per device, with that device current.  Two threads that
+    // race here both store the same address.
+    if (cudaGetSymbolAddress(&scratch, g_search_scratch) != cudaSuccess || !scratch) return SCACCHI_ECUDA;
+    g_scratch_addr[dev].store(scratch, std::memory_order_release);
+  }
+  // Every scratch byte a simulation reads is written earlier in the same
+  // simulation (the descent writes parent, action, active and the parent
+  // state of every lane; the game step writes all its outputs), so the
+  // previous call's contents need no clearing.
+  return scacchi_search_synthetic(tree, env, keys, num_simulations, max_depth, params, scratch, stats, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,97 @@
+"""scacchi_search_synthetic_static (library-owned scratch, no allocation)
+against scacchi_search_synthetic (caller workspace), both through the C
+ABI.  The two must agree bit for bit, the tolerance of every search test,
+on two calls in a row: the second call runs on scratch that still holds
+the first call's contents."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TREE_FIELDS = ("parents", "children_index", "node_to_play", "node_categorical_outcome", "node_payload",
+               "edge_categorical_outcome", "edge_payload", "node_value_priors", "node_value_alpha", "edge_alpha",
+               "invalid_actions")
+
+
+def _search(entry: str, B: int, N: int, seed: int, key_seed: int, prefix: bool):
+    from scacchi_b200 import _lib
+    from scacchi_b200 import random as R
+    from scacchi_b200.dirichlet_mctx.posterior_updates import monte_carlo_params, prefix_cdf_params
+    from scacchi_b200.dirichlet_mctx.tree import _init_tree, ptr
+    from scacchi_b200.synthetic import SyntheticGame, SyntheticGameConfig
+
+    lib = _lib.lib()
+    game = SyntheticGame(SyntheticGameConfig(seed=seed, terminal_prob=0.05))
+    root = game.root(B)
+    tree = _init_tree(root, N, ~torch.isfinite(root.prior_logits), full=False)
+    keys = torch.from_numpy(R.key_schedule(R.PRNGKey(key_seed), N)).cuda()
+    rule = (prefix_cdf_params(kappa=1.0, fallback_policy_samples=8) if prefix
+            else monte_carlo_params(kappa=4.0, policy_samples=8))
+    stats = torch.zeros(6, dtype=torch.int64, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    if entry == "workspace":
+        need = lib.scacchi_search_workspace_bytes(B, tree.A, tree.E)
+        ws = torch.empty((need,), dtype=torch.uint8, device="cuda")
+        rc = lib.scacchi_search_synthetic(tree.sref(), C.byref(game._params), ptr(keys), N, N, C.byref(rule),
+                                          ptr(ws), ptr(stats), stream)
+        held = 0
+    else:
+        torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        rc = lib.scacchi_search_synthetic_static(tree.sref(), C.byref(game._params), ptr(keys), N, N,
+                                                 C.byref(rule), ptr(stats), stream)
+        torch.cuda.synchronize()
+        held = free_before - torch.cuda.mem_get_info()[0]
+    assert rc == _lib.OK
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    out = {f: getattr(tree, f).cpu().numpy() for f in TREE_FIELDS}
+    out["stats"] = stats.cpu().numpy()
+    return out, held
+
+
+def _assert_same(a: dict, b: dict):
+    assert a.keys() == b.keys()
+    for k in a:
+        assert np.array_equal(a[k], b[k]), k
+
+
+def test_static_scratch_matches_workspace_on_two_calls_in_a_row(cuda):
+    # first call: a large batch fills most of the scratch
+    big = dict(B=4096, N=12, seed=3, key_seed=7, prefix=True)
+    _assert_same(_search("static", **big)[0], _search("workspace", **big)[0])
+    # second call: a different batch, game and rule on the stale scratch
+    # (the workspace run goes first here so that every kernel the call
+    # launches is already loaded when the device's free memory is read)
+    small = dict(B=333, N=20, seed=4, key_seed=8, prefix=False)
+    want = _search("workspace", **small)[0]
+    got, held = _search("static", **small)
+    assert held <= 0  # the call itself took no device memory
+    _assert_same(got, want)
+    assert got["stats"][0] > 0
+
+
+def test_static_scratch_rejects_batches_beyond_its_size(cuda):
+    from scacchi_b200 import _lib
+    from scacchi_b200.dirichlet_mctx.posterior_updates import prefix_cdf_params
+    from scacchi_b200.synthetic import SyntheticGameConfig
+
+    lib = _lib.lib()
+    A, E = 82, 16
+    limit = 4 << 20
+    B = 1
+    while lib.scacchi_search_workspace_bytes(B + 1, A, E) <= limit:
+        B += 1
+    assert B == 5294
+    # a tree descriptor of B + 1 lanes is rejected before any pointer is read
+    tree = _lib.ScacchiTree()
+    tree.batch, tree.num_nodes, tree.num_actions, tree.action_stride, tree.emb_bytes = B + 1, 2, A, 96, E
+    params = SyntheticGameConfig().params()
+    keys = np.zeros(8, np.uint32)
+    rc = lib.scacchi_search_synthetic_static(C.byref(tree), C.byref(params), keys.ctypes.data_as(C.c_void_p), 1, 1,
+                                             C.byref(prefix_cdf_params()), None, None)
+    assert rc == _lib.ETOOLARGE
