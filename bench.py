@@ -111,12 +111,12 @@ class ClockSampler:
                 "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
-def search_config():
+def search_config(sims: int = SIMS):
     from scacchi_b200.types import (DirichletThompsonSearchConfig, NumericalPosteriorUpdateConfig,
                                     PosteriorUpdateConfig, PosteriorUpdateKind, RootPolicySupport)
 
     return DirichletThompsonSearchConfig(
-        num_simulations=SIMS, max_depth=SIMS, root_policy_support=RootPolicySupport.search_evidence,
+        num_simulations=sims, max_depth=sims, root_policy_support=RootPolicySupport.search_evidence,
         policy_target_temperature=1.0,
         posterior_update=PosteriorUpdateConfig(
             kind=PosteriorUpdateKind.numerical,
@@ -272,6 +272,68 @@ def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
     }
 
 
+FULL_LANES = 8192
+FULL_SIMS = 256
+
+
+def full_step_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
+    """The full self-play search step on one GPU: Hex 9x9, 8192 lanes, 256
+    simulations (tree capacity 257), the 6x128 AZDirichletNet with the
+    reference's random init (zero-initialised heads) evaluating every leaf
+    on the tcgen05 tower, prefix-CDF posterior (kappa 1, Monte Carlo
+    fallback with 8 samples), exact terminal certificates, roots after 0-20
+    uniform random legal moves.  One step = one make_search(...)(roots, key)
+    call: root evaluation, 256 x (descent, Hex step, tower, expand,
+    backward), root readout and target packing."""
+    import torch
+
+    from scacchi_b200 import random as R
+    from scacchi_b200.hex import HexGame
+    from scacchi_b200.network import AZDirichletNet, init_params
+    from scacchi_b200.play_search import make_evaluator, make_search
+
+    game = HexGame(9)
+    net = AZDirichletNet(init_params(0, he_all_layers=False), fp16=fp16)
+    evaluator = make_evaluator(net)
+    tower_ms = []
+    stream = torch.cuda.current_stream()
+
+    def timed_evaluator(obs):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        out = evaluator(obs)
+        b.record(stream)
+        tower_ms.append((a, b))
+        return out
+
+    cfg = search_config(FULL_SIMS)
+    search = make_search(game, timed_evaluator, cfg)
+    state = game.random_roots(FULL_LANES, R.PRNGKey(0), 0, 20)
+    key = R.PRNGKey(1)
+    for _ in range(warmup):
+        search(state, key)
+    torch.cuda.synchronize()
+    tower_ms.clear()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        search(state, key)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    t_tower = sum(a.elapsed_time(b) for a, b in tower_ms) / steps
+    return {
+        "workload": "full search step: Hex 9x9, 8192 lanes x 256 simulations, AZDirichletNet 6x128 "
+                    "(reference random init) on the tcgen05 tower, prefix_cdf kappa 1, roots 0-20 random moves",
+        "lanes": FULL_LANES, "num_simulations": FULL_SIMS, "dtype": "fp16" if fp16 else "bf16",
+        "ms_per_step": round(ms, 2), "sims_per_s": round(FULL_LANES * FULL_SIMS / (ms / 1e3), 1),
+        "leaf_evals_per_s": round(FULL_LANES * (FULL_SIMS + 1) / (ms / 1e3), 1),
+        "tower_share": round(t_tower / ms, 4),
+        "tower_tflops": round(TOWER_FLOP_PER_BOARD * FULL_LANES * (FULL_SIMS + 1) / (t_tower / 1e3) / 1e12, 2),
+        "steps": steps, "warmup": warmup,
+    }
+
+
 def cpu_baseline(lanes: int = 384) -> dict:
     """The C oracle (a restatement of the reference's JAX path, which cannot
     be installed here) on a bounded sample: lanes [0, lanes) of the same
@@ -340,8 +402,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="search", choices=["search", "tower"],
-                    help="search: the isolated search kernels (default); tower: the residual tower alone")
+    ap.add_argument("--workload", default="search", choices=["search", "tower", "full"],
+                    help="search: the isolated search kernels (default); tower: the residual tower alone; "
+                         "full: the full Hex search step with the tower evaluating leaves")
     ap.add_argument("--fp16", action="store_true", help="tower: fp16 operands instead of bf16")
     ap.add_argument("--profile", action="store_true",
                     help="profiling mode: warmup steps + one device-resident step, no JSON line "
@@ -382,6 +445,18 @@ def main() -> None:
                               "config": {"workload": "residual tower alone: 6x128 ResNet, 9x9x4 {0,1} planes "
                                                      "(density 0.4), He-normal weights seed 0", "boards": TOWER_BOARDS},
                               "tflops": t["tflops"], "roofline": t["roofline"]}), flush=True)
+        return
+    if args.workload == "full":
+        if rank == 0:
+            f = full_step_bench(args.steps, args.warmup, args.fp16)
+            print(json.dumps({"metric": METRIC, "value": f["sims_per_s"], "unit": "sims/s", "n_gpus": 1,
+                              "steps": args.steps, "warmup": args.warmup, "ms_per_step": f["ms_per_step"],
+                              "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                              "dtype": f["dtype"], "data": "synthetic",
+                              "config": {"workload": f["workload"], "lanes": FULL_LANES,
+                                         "num_simulations": FULL_SIMS},
+                              "leaf_evals_per_s": f["leaf_evals_per_s"], "tower_share": f["tower_share"],
+                              "tower_tflops": f["tower_tflops"]}), flush=True)
         return
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
@@ -502,6 +577,7 @@ def main() -> None:
         }
         if world == 1:
             line["tower"] = tower_bench(5, 3)
+            line["full_step"] = full_step_bench(3, 3)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

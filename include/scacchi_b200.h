@@ -266,6 +266,50 @@ int scacchi_search_synthetic_static(const scacchi_tree *tree, const scacchi_synt
                                     const uint32_t *keys, int32_t num_simulations, int32_t max_depth,
                                     const scacchi_update_params *params, uint64_t *stats, void *stream);
 
+/* ---- Hex environment (envs.py:98-125 over pgx 2.6.0 Hex) -------------- */
+
+/* A lane's state is a 48-byte record: black and white bitboards (bit
+ * r * size + c of two little-endian uint64 words each), then colour to move
+ * (0 black), the player id playing black, terminated, the winning colour
+ * (int8, -1 none), size and stones placed.  Actions are the size * size
+ * cells plus a swap action (index size * size) that is never legal.
+ * Observations are float32 [B, size, size, 4] for the player to move: own
+ * stones, opponent stones, own colour, 1 on the second move. */
+#define SCACCHI_HEX_RECORD_BYTES 48
+
+/* env.init (envs.py:103-112) per lane key uint32[B, 2]. */
+int scacchi_hex_init(int32_t batch, int32_t size, const uint32_t *keys, uint8_t *states, void *stream);
+
+/* Seeded roots of the full-step workload: per lane, a random player order
+ * and min_moves..max_moves uniform random legal moves from the empty
+ * board (no reference counterpart). */
+int scacchi_hex_random_roots(int32_t batch, int32_t size, uint32_t key0, uint32_t key1, int32_t min_moves,
+                             int32_t max_moves, uint8_t *states, void *stream);
+
+/* env.step (envs.py:114-123) fused with the recurrent function's
+ * derivations (dirichlet_q_search.py:43-76): next_states [B, 48] and,
+ * for each non-NULL output, the child's observation, invalid actions
+ * [B, size*size + 1], terminal outcome aligned to the child's player (-1
+ * when not terminal), player to move, rewards [B, 2] and terminated.  An
+ * illegal action or a terminal parent leaves the state unchanged (the
+ * search steps lanes with nothing to expand with action 0 and discards
+ * their results); a record whose size is out of range sets bit 0 of
+ * scacchi_hex_error() and writes nothing for that lane. */
+int scacchi_hex_step(int32_t batch, const uint8_t *states, const int32_t *action, uint8_t *next_states,
+                     float *observation, uint8_t *invalid, int8_t *terminal_outcome, int32_t *to_play,
+                     float *rewards, uint8_t *terminated, void *stream);
+
+/* The same outputs for given states (roots): the terminal outcome is from
+ * the perspective of the state's own player to move. */
+int scacchi_hex_observe(int32_t batch, const uint8_t *states, float *observation, uint8_t *invalid,
+                        int8_t *terminal_outcome, int32_t *to_play, float *rewards, uint8_t *terminated,
+                        void *stream);
+
+/* Sticky Hex error flags (bit 0: a record with an out-of-range size;
+ * reading synchronises and clears) and launches. */
+int scacchi_hex_error(uint32_t *flags);
+uint64_t scacchi_hex_launch_count(void);
+
 /* ---- leaf evaluation: AZDirichletNet (network.py:338-524) -------------- */
 
 /* Inference weights of the 9x9 resnet_v2 AZDirichletNet with binary

@@ -87,6 +87,12 @@ SIGNATURES = {
     "scacchi_key_schedule": [C.c_uint32, C.c_uint32, I32, P],
     "scacchi_split_host": [C.c_uint32, C.c_uint32, I32, P],
     "scacchi_fold_in_host": [C.c_uint32, C.c_uint32, C.c_uint32, P],
+    "scacchi_hex_init": [I32, I32, P, P, P],
+    "scacchi_hex_random_roots": [I32, I32, C.c_uint32, C.c_uint32, I32, I32, P, P],
+    "scacchi_hex_step": [I32, P, P, P, P, P, P, P, P, P, P],
+    "scacchi_hex_observe": [I32, P, P, P, P, P, P, P, P],
+    "scacchi_hex_error": [P],
+    "scacchi_hex_launch_count": [],
     "scacchi_tower_rows": [I32],
     "scacchi_tower_workspace_bytes": [I32],
     "scacchi_tower_forward": [C.POINTER(TowerWeights), P, I32, P, P, P, P, P, P, P],
@@ -98,7 +104,7 @@ SIGNATURES = {
 }
 RESTYPES = {"scacchi_search_workspace_bytes": C.c_size_t, "scacchi_launch_count": C.c_uint64,
             "scacchi_tower_rows": C.c_uint64, "scacchi_tower_workspace_bytes": C.c_size_t,
-            "scacchi_tower_launch_count": C.c_uint64}
+            "scacchi_tower_launch_count": C.c_uint64, "scacchi_hex_launch_count": C.c_uint64}
 
 
 class ScacchiError(RuntimeError):
@@ -139,8 +145,9 @@ def device_error() -> int:
 
 
 def launch_count() -> int:
-    """Kernels this library launched since load (search + network)."""
-    return int(lib().scacchi_launch_count()) + int(lib().scacchi_tower_launch_count())
+    """Kernels this library launched since load (search + network + Hex)."""
+    return (int(lib().scacchi_launch_count()) + int(lib().scacchi_tower_launch_count())
+            + int(lib().scacchi_hex_launch_count()))
 
 
 def tower_error() -> int:

@@ -555,9 +555,12 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
   }
 }
 
-// backward (search.py:146-171) with the built-in rules, one CTA per lane
+// backward (search.py:146-171) with the built-in rules, one CTA per lane.
+// Shared memory already limits the 3-warp instance to 6 CTAs per SM; a
+// register budget for 5 keeps the kernel free of spills (tighter budgets
+// spill 60-120 bytes per thread and measured no faster).
 #ifndef SCACCHI_BWD_MIN_BLOCKS
-#define SCACCHI_BWD_MIN_BLOCKS 8
+#define SCACCHI_BWD_MIN_BLOCKS 5
 #endif
 
 template <int W>
