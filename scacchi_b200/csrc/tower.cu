@@ -12,14 +12,23 @@
 //
 //   out[r, n] = sum_t sum_c act[r + off_t, c] * W[t, n, c],  K = 9 * 128.
 //
-// conv_tc_kernel: persistent (one CTA per SM), warp-specialised
-//   warp 0      TMA producer: A (128 rows x 64 ch) + B (128 out x 64 in) per
-//               K block, 4-stage mbarrier ring
+// conv_tc_kernel: persistent (one CTA per SM), warp-specialised, over tile
+// pairs of 256 rows.  The nine taps of a pair read overlapping row ranges,
+// so A is loaded once per pair and 64-channel half as a 288-row window
+// (shared memory traffic per pair: 72 KB of A instead of 18 x 32 KB), and
+// each weight tile feeds both 128-row accumulators of the pair.
+//   warp 0      TMA producer of the weights: the nine (tap, h) tiles (128
+//               out x 64 in) per half through a 4-stage ring
+//   warp 10     TMA producer of the windows: half h of the next pair loads
+//               as soon as the MMAs finish reading half h of this one
 //   warp 1      TMEM allocator and MMA issuer (one thread):
 //               tcgen05.mma.cta_group::1.kind::f16, M = N = 128, K = 16,
-//               bf16 x bf16 -> fp32 accumulated in TMEM (two 128-column
-//               accumulators so the epilogue of tile i overlaps tile i+1)
-//   warps 2-5   epilogue: tcgen05.ld 32x32b, fused bias / folded BatchNorm /
+//               16-bit operands -> fp32 in TMEM; a tap's A matrix starts at
+//               window row 16 + 128 * sub + shift (any row: the swizzle
+//               phase follows the address); four 128-column
+//               accumulators, so a pair's epilogue overlaps the next pair
+//   warps 2-9   epilogue, two warps per TMEM lane quadrant (64 columns
+//               each): tcgen05.ld 32x32b, fused bias / folded BatchNorm /
 //               ReLU / residual / next block's BN-ReLU, bf16 into
 //               128B-swizzled shared memory, TMA store; the last layer
 //               instead computes the heads' 1x1 convolutions per row.
@@ -42,13 +51,22 @@ namespace {
 
 constexpr int kC = 128;          // channels
 constexpr int kRowsPerBoard = 100;
-constexpr int kBM = 128;         // rows per tile
-constexpr int kBK = 64;          // channels per K block (128 bytes of bf16)
-constexpr int kKBlocks = 18;     // 9 taps x 2 channel blocks
-constexpr int kStages = 4;
+constexpr int kBM = 128;         // rows per accumulator tile
+constexpr int kBK = 64;          // channels per K block (128 bytes of 16-bit values)
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB
-constexpr int kStageBytes = 2 * kTileBytes;
-constexpr int kThreads = 192;
+#ifndef SCACCHI_CONV_BSTAGES
+#define SCACCHI_CONV_BSTAGES 4
+#endif
+constexpr int kBStages = SCACCHI_CONV_BSTAGES;  // weight tiles in flight
+constexpr int kBTileBytes = kC * kBK * 2;  // 16 KB: 128 outputs x 64 inputs of one tap
+constexpr int kWinLead = 16;     // window rows above (and below) a tile pair: taps shift by <= 11
+constexpr int kWinRows = 2 * kBM + 2 * kWinLead;    // 288
+constexpr int kWinBoxRows = kWinRows / 2;           // 144 rows per TMA box (<= 256)
+constexpr int kWinHalfBytes = kWinRows * kBK * 2;   // 36 KB per 64-channel half
+constexpr int kTmemCols = 512;   // two pairs of 128-column accumulators
+constexpr int kEpiWarps = 8;     // two per TMEM lane quadrant, 64 columns each
+constexpr int kEpiThreads = 32 * kEpiWarps;
+constexpr int kThreads = 64 + kEpiThreads + 32;  // + the window producer warp
 constexpr int kHeadCh = 6;       // policy 2, value 1, q mean 2, q concentration 1
 constexpr uint32_t kWaitLimit = 1u << 30;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
@@ -194,7 +212,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 }
 
 // shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (leading offset unused for swizzled K-major layouts)
+// 1024 bytes apart (leading offset unused for swizzled K-major layouts).  A
+// matrix may start at any 128-byte row of a 1024-byte-aligned swizzled
+// tile with the base-offset field (bits 49-51) left at zero: the MMA takes
+// the swizzle phase from the address bits themselves, as TMA does when it
+// writes the tile (measured on B200: setting the field to the start's phase
+// gives wrong products).
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
@@ -266,18 +289,123 @@ struct EpiParams {
   float *head_out;           // heads: [rows, 8] f32
 };
 
+// Shared memory of conv_tc_kernel.  A tile pair is 256 output rows (two
+// 128-row accumulators sharing every weight tile).  Its A operand for all
+// nine taps is one window of 288 input rows (16 above the pair, 16 below;
+// taps shift by at most 11) per 64-channel half, loaded once; a tap's A
+// matrix is the window read from row 16 + 128 * sub + shift.  Weights
+// stream through a ring of 16 KB (tap, half) tiles.
 struct SmemLayout {
-  static constexpr int kStagesOff = 0;
-  static constexpr int kOutOff = kStages * kStageBytes;               // 2 outputs x 2 halves x 16 KB
+  static constexpr int kWinOff = 0;                                    // 2 halves x 36 KB
+  static constexpr int kBOff = kWinOff + 2 * kWinHalfBytes;
+  static constexpr int kOutOff = kBOff + kBStages * kBTileBytes;       // 2 outputs x 2 halves x 16 KB
   static constexpr int kParamOff = kOutOff + 4 * kTileBytes;           // floats
   static constexpr int kParamFloats = 3 * kC + kHeadCh * kC + 8;
-  static constexpr int kBarOff = kParamOff + kParamFloats * 4;
-  static constexpr int kBytes = kBarOff + 8 * (2 * kStages + 4) + 16 + 1024;  // + alignment slack
-
+  static constexpr int kHeadPartOff = kParamOff + kParamFloats * 4;  // [128 rows][kHeadCh] floats
+  static constexpr int kBarOff = kHeadPartOff + kBM * kHeadCh * 4;
+  static constexpr int kNumBars = 2 + 2 + 2 * kBStages + 2 + 2;
+  static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
 };
+static_assert(SmemLayout::kBOff % 1024 == 0 && SmemLayout::kOutOff % 1024 == 0, "swizzled tiles 1024-aligned");
+static_assert(SmemLayout::kBytes <= 227 * 1024, "shared memory budget");
+
+// One 128-row accumulator of a tile: bias / folded BatchNorm / ReLU /
+// residual / next block's BN-ReLU, 16-bit outputs staged 128B-swizzled for
+// the TMA store, or the heads' 1x1 convolutions per row.  Each thread owns
+// one row of the tile (its warp's TMEM lane quadrant) and 64 of the 128
+// columns (`half`); the two warps of a quadrant split the columns.  `head`
+// returns the row's partial head sums over its columns.
+template <typename T>
+__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const float *prm, uint32_t acc_addr, int tile,
+                                              int quad, int half, int lane, uint8_t *out0, uint8_t *out1,
+                                              float (&head)[kHeadCh]) {
+  const int row_in_tile = quad * 32 + lane;
+  const int r = tile * kBM + row_in_tile;
+  const int p = r % kRowsPerBoard;
+  const bool real = r < ep.rows_valid && p >= 10 && (p % 10) != 9;
+#pragma unroll
+  for (int h = 0; h < kHeadCh; ++h) head[h] = 0.0f;
+  for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
+    // the residual's global loads go out before the accumulator read waits
+    uint4 ru[4];
+    if (ep.mode != kEpiConv1) {
+      const uint4 *src =
+          reinterpret_cast<const uint4 *>(static_cast<const T *>(ep.residual) + (size_t)r * kC + ch * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ru[q] = real ? src[q] : make_uint4(0, 0, 0, 0);
+    }
+    float v[32];
+    tmem_ld32(acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ch * 32), v);
+    float res[32];
+    if (ep.mode != kEpiConv1) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const T *hb = reinterpret_cast<const T *>(&ru[q]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) res[q * 8 + e] = F16Traits<T>::to_f(hb[e]);
+      }
+    }
+    uint32_t pk0[16], pk1[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float o0[2], o1[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int n = ch * 32 + i + j;
+        float y = v[i + j] + prm[n];
+        if (ep.mode == kEpiConv1) {
+          y = real ? fmaxf(y, 0.0f) : 0.0f;
+          o0[j] = y;
+          o1[j] = 0.0f;
+        } else {
+          // residual stream stored in the 16-bit type like the reference's bf16 model
+          const float xn = F16Traits<T>::to_f(F16Traits<T>::from_f(y + res[i + j]));
+          const float a = fmaxf(fmaf(xn, prm[kC + n], prm[2 * kC + n]), 0.0f);
+          o0[j] = real ? xn : 0.0f;
+          o1[j] = real ? F16Traits<T>::to_f(F16Traits<T>::from_f(a)) : 0.0f;
+          if (ep.mode == kEpiHeads) {
+#pragma unroll
+            for (int h = 0; h < kHeadCh; ++h) head[h] = fmaf(o1[j], prm[3 * kC + h * kC + n], head[h]);
+          }
+        }
+      }
+      pk0[i / 2] = F16Traits<T>::pack(o0[0], o0[1]);
+      pk1[i / 2] = F16Traits<T>::pack(o1[0], o1[1]);
+    }
+    if (ep.mode != kEpiHeads) {
+      // 32 channels = four 16-byte chunks of the 64-channel half `ch / 2`
+      uint8_t *h0 = out0 + (ch >> 1) * kTileBytes;
+      uint8_t *h1 = out1 + (ch >> 1) * kTileBytes;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = (ch & 1) * 4 + q;
+        *reinterpret_cast<uint4 *>(h0 + swz(row_in_tile, chunk)) =
+            make_uint4(pk0[4 * q], pk0[4 * q + 1], pk0[4 * q + 2], pk0[4 * q + 3]);
+        if (ep.mode == kEpiConv2)
+          *reinterpret_cast<uint4 *>(h1 + swz(row_in_tile, chunk)) =
+              make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
+      }
+    }
+  }
+}
+
+// heads: the row's two column halves' partial sums, bias, ReLU
+__device__ __forceinline__ void store_heads(const EpiParams &ep, const float *prm, int tile, int row_in_tile,
+                                            const float (&lo)[kHeadCh], const float *hi) {
+  const int r = tile * kBM + row_in_tile;
+  if (r >= ep.rows_valid) return;
+  const int p = r % kRowsPerBoard;
+  const bool real = p >= 10 && (p % 10) != 9;
+  float hb[kHeadCh];
+#pragma unroll
+  for (int h = 0; h < kHeadCh; ++h) hb[h] = real ? fmaxf(lo[h] + hi[h] + prm[3 * kC + kHeadCh * kC + h], 0.0f) : 0.0f;
+  float4 *dst = reinterpret_cast<float4 *>(ep.head_out + (size_t)r * 8);
+  dst[0] = make_float4(hb[0], hb[1], hb[2], hb[3]);
+  dst[1] = make_float4(hb[4], hb[5], 0.0f, 0.0f);
+}
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ CUtensorMap tm_in,
+__global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ CUtensorMap tm_win,
                                                               const __grid_constant__ CUtensorMap tm_w,
                                                               const __grid_constant__ CUtensorMap tm_out0,
                                                               const __grid_constant__ CUtensorMap tm_out1,
@@ -285,10 +413,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int num_pairs = (num_tiles + 1) / 2;
   float *prm = reinterpret_cast<float *>(smem + SmemLayout::kParamOff);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + SmemLayout::kBarOff);
-  uint64_t *empty = full + kStages;
-  uint64_t *acc_full = empty + kStages;
+  uint64_t *win_full = reinterpret_cast<uint64_t *>(smem + SmemLayout::kBarOff);
+  uint64_t *win_empty = win_full + 2;
+  uint64_t *b_full = win_empty + 2;
+  uint64_t *b_empty = b_full + kBStages;
+  uint64_t *acc_full = b_empty + kBStages;
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -304,19 +435,23 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     if (threadIdx.x < kHeadCh) prm[3 * kC + kHeadCh * kC + threadIdx.x] = ep.head_b[threadIdx.x];
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&win_full[h], 1);
+      mbar_init(&win_empty[h], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&b_full[s], 1);
+      mbar_init(&b_empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], kEpiThreads);
     }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 256);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -325,187 +460,174 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- weight producer ----------------
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_mask = 0, issued_parity = 0;  // per stage: issued?, parity of the last load
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        const int row0 = tile * kBM;
-        for (int kb = 0; kb < kKBlocks; ++kb) {
-          const int tap = kb >> 1, cb = kb & 1;
-          const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
-          uint8_t *sa = smem + SmemLayout::kStagesOff + stage * kStageBytes;
-          mbar_expect_tx(&full[stage], kStageBytes);
-          tma_load_2d(sa, &tm_in, &full[stage], cb * kBK, row0 + off);
-          tma_load_2d(sa + kTileBytes, &tm_w, &full[stage], cb * kBK, tap * kC);
-          issued_mask |= 1u << stage;
-          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+      int bstage = 0;
+      uint32_t bphase = 0, b_issued = 0, b_parity = 0;  // per stage: issued?, parity of the last load
+      bool stop = false;
+      for (int pair = blockIdx.x; pair < num_pairs && !stop && !*abort_flag; pair += gridDim.x) {
+        for (int h = 0; h < 2 && !stop; ++h) {
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&b_empty[bstage], bphase ^ 1u, abort_flag)) {
+              stop = true;
+              break;
+            }
+            uint8_t *sb = smem + SmemLayout::kBOff + bstage * kBTileBytes;
+            mbar_expect_tx(&b_full[bstage], kBTileBytes);
+            tma_load_2d(sb, &tm_w, &b_full[bstage], h * kBK, tap * kC);
+            b_issued |= 1u << bstage;
+            b_parity = (b_parity & ~(1u << bstage)) | (bphase << bstage);
+            if (++bstage == kBStages) {
+              bstage = 0;
+              bphase ^= 1u;
+            }
           }
         }
       }
       // every load issued into shared memory lands before the CTA may exit
-      for (int s = 0; s < kStages; ++s) {
-        if (!(issued_mask >> s & 1u)) continue;
-        mbar_drain(&full[s], issued_parity >> s & 1u);
+      for (int s = 0; s < kBStages; ++s)
+        if (b_issued >> s & 1u) mbar_drain(&b_full[s], b_parity >> s & 1u);
+    }
+  } else if (warp == kThreads / 32 - 1) {
+    // ---------------- window producer ----------------
+    // Its own warp, so a window half reloads as soon as the MMAs release it
+    // (a whole half of the pair ahead) instead of queueing behind weights.
+    if (lane == 0) {
+      uint32_t wphase[2] = {0u, 0u}, w_issued = 0, w_parity = 0;
+      bool stop = false;
+      for (int pair = blockIdx.x; pair < num_pairs && !stop && !*abort_flag; pair += gridDim.x) {
+        const int row0 = pair * 2 * kBM;
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&win_empty[h], wphase[h] ^ 1u, abort_flag)) {
+            stop = true;
+            break;
+          }
+          uint8_t *win = smem + SmemLayout::kWinOff + h * kWinHalfBytes;
+          mbar_expect_tx(&win_full[h], kWinHalfBytes);
+          tma_load_2d(win, &tm_win, &win_full[h], h * kBK, row0 - kWinLead);
+          tma_load_2d(win + kWinBoxRows * 128, &tm_win, &win_full[h], h * kBK, row0 - kWinLead + kWinBoxRows);
+          w_issued |= 1u << h;
+          w_parity = (w_parity & ~(1u << h)) | (wphase[h] << h);
+          wphase[h] ^= 1u;
+        }
       }
+      for (int h = 0; h < 2; ++h)
+        if (w_issued >> h & 1u) mbar_drain(&win_full[h], w_parity >> h & 1u);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag)) break;
+      int bstage = 0, slot = 0;
+      uint32_t bphase = 0, acc_phase = 0, wphase[2] = {0u, 0u};
+      for (int pair = blockIdx.x; pair < num_pairs && !*abort_flag; pair += gridDim.x) {
+        if (!mbar_wait(&acc_empty[slot], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(acc * kC);
+        const uint32_t d0 = tmem_base + (uint32_t)(2 * slot * kC);
         bool ok = true;
-        for (int kb = 0; kb < kKBlocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!mbar_wait(&win_full[h], wphase[h], abort_flag)) {
             ok = false;
             break;
           }
+          wphase[h] ^= 1u;
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + SmemLayout::kStagesOff + stage * kStageBytes);
-          const uint32_t sb = sa + kTileBytes;
+          const uint32_t win = smem_u32(smem + SmemLayout::kWinOff + h * kWinHalfBytes);
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!mbar_wait(&b_full[bstage], bphase, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sb = smem_u32(smem + SmemLayout::kBOff + bstage * kBTileBytes);
+            const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t adesc = smem_desc_sw128(sa + k * 32);
-            const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
-            umma_f16(d, adesc, bdesc, idesc_for<T>(), (kb | k) != 0);
+            for (int sub = 0; sub < 2; ++sub) {
+              const int w = kWinLead + sub * kBM + off;  // window row of the sub-tile's row 0
+#pragma unroll
+              for (int k = 0; k < kBK / 16; ++k) {
+                const uint64_t adesc = smem_desc_sw128(win + (uint32_t)w * 128u + k * 32);
+                const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
+                umma_f16(d0 + (uint32_t)(sub * kC), adesc, bdesc, idesc_for<T>(), (h | tap | k) != 0);
+              }
+            }
+            umma_commit(&b_empty[bstage]);
+            if (++bstage == kBStages) {
+              bstage = 0;
+              bphase ^= 1u;
+            }
           }
-          umma_commit(&empty[stage]);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (ok) umma_commit(&win_empty[h]);
         }
         if (!ok) break;
-        umma_commit(&acc_full[acc]);
-        if (++acc == 2) {
-          acc = 0;
+        umma_commit(&acc_full[slot]);
+        if (++slot == 2) {
+          slot = 0;
           acc_phase ^= 1u;
         }
       }
     }
   } else {
-    // ---------------- epilogue (warps 2-5) ----------------
+    // ---------------- epilogue (warps 2-9) ----------------
     const int quad = warp & 3;              // TMEM lanes this warp may access
-    const int row_in_tile = quad * 32 + lane;
-    const int et = threadIdx.x - 64;        // 0..127
+    const int half = (warp - 2) >> 2;       // column half: warps 2-5 -> 0, 6-9 -> 1
+    const int et = threadIdx.x - 64;        // 0..255
     uint8_t *out0 = smem + SmemLayout::kOutOff;
     uint8_t *out1 = out0 + 2 * kTileBytes;
-    volatile int *go = abort_flag + 1;  // elected thread's verdict for the tile
-    int acc = 0;
+    float *head_part = reinterpret_cast<float *>(smem + SmemLayout::kHeadPartOff);
+    volatile int *go = abort_flag + 1;  // elected thread's verdict for the pair
+    int slot = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      // one thread waits (bounded) and broadcasts, so the 128 threads agree
+    for (int pair = blockIdx.x; pair < num_pairs; pair += gridDim.x) {
+      // one thread waits (bounded) and broadcasts, so the epilogue threads agree
       if (et == 0) {
-        const bool ok = !*abort_flag && mbar_wait(&acc_full[acc], acc_phase, abort_flag);
-        // staging buffers must be free (previous tile's TMA store read them)
-        tma_store_wait_read();
+        const bool ok = !*abort_flag && mbar_wait(&acc_full[slot], acc_phase, abort_flag);
         *go = ok ? 1 : 0;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
       if (!*go) break;
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // everyone read `go` before it changes
+      asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");  // everyone read `go` before it changes
       tc_fence_after();
-      const int r = tile * kBM + row_in_tile;
-      const int p = r % kRowsPerBoard;
-      const bool real = r < ep.rows_valid && p >= 10 && (p % 10) != 9;
-      float head[kHeadCh];
-#pragma unroll
-      for (int h = 0; h < kHeadCh; ++h) head[h] = 0.0f;
-      for (int ch = 0; ch < 4; ++ch) {
-        float v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * kC + ch * 32), v);
-        float res[32];
-        if (ep.mode != kEpiConv1) {
-          const uint4 *src =
-              reinterpret_cast<const uint4 *>(static_cast<const T *>(ep.residual) + (size_t)r * kC + ch * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 u = real ? src[q] : make_uint4(0, 0, 0, 0);
-            const T *hb = reinterpret_cast<const T *>(&u);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) res[q * 8 + e] = F16Traits<T>::to_f(hb[e]);
-          }
-        }
-        uint32_t pk0[16], pk1[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float o0[2], o1[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int n = ch * 32 + i + j;
-            float y = v[i + j] + prm[n];
-            if (ep.mode == kEpiConv1) {
-              y = real ? fmaxf(y, 0.0f) : 0.0f;
-              o0[j] = y;
-              o1[j] = 0.0f;
-            } else {
-              // residual stream stored in the 16-bit type like the reference's bf16 model
-              const float xn = F16Traits<T>::to_f(F16Traits<T>::from_f(y + res[i + j]));
-              const float a = fmaxf(fmaf(xn, prm[kC + n], prm[2 * kC + n]), 0.0f);
-              o0[j] = real ? xn : 0.0f;
-              o1[j] = real ? F16Traits<T>::to_f(F16Traits<T>::from_f(a)) : 0.0f;
-              if (ep.mode == kEpiHeads) {
-#pragma unroll
-                for (int h = 0; h < kHeadCh; ++h) head[h] = fmaf(o1[j], prm[3 * kC + h * kC + n], head[h]);
-              }
-            }
-          }
-          pk0[i / 2] = F16Traits<T>::pack(o0[0], o0[1]);
-          pk1[i / 2] = F16Traits<T>::pack(o1[0], o1[1]);
-        }
+      for (int sub = 0; sub < 2; ++sub) {
+        const int tile = pair * 2 + sub;
+        if (tile >= num_tiles) break;  // uniform across the epilogue threads
         if (ep.mode != kEpiHeads) {
-          // 32 channels = four 16-byte chunks of the 64-channel half `ch / 2`
-          uint8_t *h0 = out0 + (ch >> 1) * kTileBytes;
-          uint8_t *h1 = out1 + (ch >> 1) * kTileBytes;
+          // the staging buffers are free once the previous store has read them
+          if (et == 0) tma_store_wait_read();
+          asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+        }
+        float head[kHeadCh];
+        epilogue_tile<T>(ep, prm, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0, out1,
+                         head);
+        if (ep.mode == kEpiHeads) {
+          const int row_in_tile = quad * 32 + lane;
+          if (half == 1) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = (ch & 1) * 4 + q;
-            *reinterpret_cast<uint4 *>(h0 + swz(row_in_tile, chunk)) =
-                make_uint4(pk0[4 * q], pk0[4 * q + 1], pk0[4 * q + 2], pk0[4 * q + 3]);
-            if (ep.mode == kEpiConv2)
-              *reinterpret_cast<uint4 *>(h1 + swz(row_in_tile, chunk)) =
-                  make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
+            for (int h = 0; h < kHeadCh; ++h) head_part[row_in_tile * kHeadCh + h] = head[h];
           }
+          asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+          if (half == 0) store_heads(ep, prm, tile, row_in_tile, head, head_part + row_in_tile * kHeadCh);
+          asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");  // partials consumed
+          continue;
+        }
+        fence_proxy_async();
+        asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
+        if (et == 0) {
+          const int row0 = tile * kBM;
+          tma_store_2d(&tm_out0, out0, 0, row0);
+          tma_store_2d(&tm_out0, out0 + kTileBytes, kBK, row0);
+          if (ep.mode == kEpiConv2) {
+            tma_store_2d(&tm_out1, out1, 0, row0);
+            tma_store_2d(&tm_out1, out1 + kTileBytes, kBK, row0);
+          }
+          tma_store_commit();
         }
       }
-      // the accumulator can be reused by the MMA warp
+      // both accumulators of the pair can be reused by the MMA warp
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
-      if (++acc == 2) {
-        acc = 0;
+      mbar_arrive(&acc_empty[slot]);
+      if (++slot == 2) {
+        slot = 0;
         acc_phase ^= 1u;
-      }
-      if (ep.mode == kEpiHeads) {
-        if (r < ep.rows_valid) {
-          float4 *dst = reinterpret_cast<float4 *>(ep.head_out + (size_t)r * 8);
-          float hb[kHeadCh];
-#pragma unroll
-          for (int h = 0; h < kHeadCh; ++h) hb[h] = real ? fmaxf(head[h] + prm[3 * kC + kHeadCh * kC + h], 0.0f) : 0.0f;
-          dst[0] = make_float4(hb[0], hb[1], hb[2], hb[3]);
-          dst[1] = make_float4(hb[4], hb[5], 0.0f, 0.0f);
-        }
-        continue;
-      }
-      fence_proxy_async();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) {
-        const int row0 = tile * kBM;
-        tma_store_2d(&tm_out0, out0, 0, row0);
-        tma_store_2d(&tm_out0, out0 + kTileBytes, kBK, row0);
-        if (ep.mode == kEpiConv2) {
-          tma_store_2d(&tm_out1, out1, 0, row0);
-          tma_store_2d(&tm_out1, out1 + kTileBytes, kBK, row0);
-        }
-        tma_store_commit();
       }
     }
     if (et == 0) tma_store_wait_all();
@@ -518,55 +640,166 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, 256);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
 // ---------------------------------------------------------------------------
-// stem: conv3x3 in_planes -> 128 (+ bias), then BN1 of block 0 and ReLU
+// stem: conv3x3 in_planes -> 128 (+ bias), then BN1 of block 0 and ReLU.
+// A CTA serves kStemBoards boards; each thread computes 8 adjacent
+// channels of one row (16 threads cover a row, so a warp stores two full
+// 256-byte rows per output).  For observations of {0, 1} planes (at most
+// 4) the CTA first tabulates, per tap, the weight sum of each of the 16
+// plane subsets, so a tap costs one table row instead of a product per
+// plane; other inputs take the direct products.
 // ---------------------------------------------------------------------------
 
+constexpr int kStemBoards = 8;
+constexpr int kStemThreads = 256;
+constexpr int kStemSubsets = 16;  // plane subsets of up to 4 planes
+
+size_t stem_smem_bytes(int in_planes) {
+  const int rows = 9 * (in_planes <= 4 ? kStemSubsets : in_planes);
+  return (size_t)rows * kC * sizeof(float) + kStemBoards * 128;
+}
+
 template <typename T>
-__global__ void stem_kernel(const float *obs, int in_planes, const float *w, const float *b, const float *s1,
-                            const float *t1, T *x, T *a) {
+__global__ void __launch_bounds__(kStemThreads, 2) stem_kernel(const float *obs, int boards, int in_planes,
+                                                            const float *w, const float *b, const float *s1,
+                                                            const float *t1, T *x, T *a) {
   extern __shared__ float sm[];
-  const int e = blockIdx.x, n = threadIdx.x;
-  float *so = sm;                       // [9*9*in_planes]
-  float *sw = sm + 81 * in_planes;      // [9 * in_planes][128]
-  for (int i = n; i < 81 * in_planes; i += blockDim.x) so[i] = obs[(size_t)e * 81 * in_planes + i];
-  for (int i = n; i < 9 * in_planes * kC; i += blockDim.x) sw[i] = w[i];
-  __syncthreads();
-  const float bias = b[n], sc = s1[n], sh = t1[n];
-  for (int p = 0; p < kRowsPerBoard; ++p) {
-    const int yp = p / 10, xp = p % 10;
+  const bool table = in_planes <= 4;
+  // table: [9 taps][16 subsets][128]; otherwise the weights [9 * in_planes][128]
+  float *sw = sm;
+  uint8_t *masks = reinterpret_cast<uint8_t *>(sm + 9 * (table ? kStemSubsets : in_planes) * kC);  // [boards][11 * 11]
+  const int e0 = blockIdx.x * kStemBoards;
+  const int nb = min(kStemBoards, boards - e0);
+  if (table) {
+    // a table row keeps channel n = 8 g + 4 j + l at 64 j + 4 g + l, so the
+    // 16 threads of a row read 256 contiguous bytes per float4 load
+    for (int i = threadIdx.x; i < 9 * kStemSubsets * kC; i += kStemThreads) {
+      const int k = i % kC, m = (i / kC) % kStemSubsets, tap = i / (kStemSubsets * kC);
+      const int n = ((k & 63) >> 2) * 8 + (k >> 6) * 4 + (k & 3);
+      float v = 0.0f;
+      bool any = false;
+      for (int c = 0; c < in_planes; ++c)
+        if (m >> c & 1) {
+          const float wv = w[(tap * in_planes + c) * kC + n];
+          v = any ? v + wv : wv;
+          any = true;
+        }
+      sw[i] = v;  // subsets naming planes >= in_planes are never looked up
+    }
+  } else {
+    for (int i = threadIdx.x; i < 9 * in_planes * kC; i += kStemThreads) sw[i] = w[i];
+  }
+  // plane-subset mask per cell on an 11 x 11 grid with a zero border
+  int binary = table ? 1 : 0;
+  if (table) {
+    for (int i = threadIdx.x; i < nb * 121; i += kStemThreads) {
+      const int eb = i / 121, q = i % 121, yy = q / 11 - 1, xx = q % 11 - 1;
+      uint32_t m = 0;
+      if (yy >= 0 && yy < 9 && xx >= 0 && xx < 9) {
+        const float *o = obs + ((size_t)(e0 + eb) * 81 + yy * 9 + xx) * in_planes;
+        for (int c = 0; c < in_planes; ++c) {
+          const float v = o[c];
+          if (v == 1.0f) m |= 1u << c;
+          else if (v != 0.0f) binary = 0;
+        }
+      }
+      masks[eb * 128 + q] = (uint8_t)m;
+    }
+  }
+  binary = __syncthreads_and(binary);
+  const int g = threadIdx.x & 15, n0 = g * 8;  // this thread's 8 channels
+  float bias[8], sc[8], sh[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    bias[j] = b[n0 + j];
+    sc[j] = s1[n0 + j];
+    sh[j] = t1[n0 + j];
+  }
+  for (int item = threadIdx.x >> 4; item < kStemBoards * kRowsPerBoard; item += kStemThreads >> 4) {
+    const int eb = item / kRowsPerBoard, p = item - eb * kRowsPerBoard;
+    if (eb >= nb) break;
+    const int yp = p / 10, xp = p - yp * 10;
     const bool real = yp >= 1 && xp <= 8;
-    float acc = bias;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = bias[j];
     if (real) {
       const int y = yp - 1, xx = xp;
-      for (int ky = 0; ky < 3; ++ky) {
-        const int iy = y + ky - 1;
-        if (iy < 0 || iy >= 9) continue;
-        for (int kx = 0; kx < 3; ++kx) {
-          const int ix = xx + kx - 1;
-          if (ix < 0 || ix >= 9) continue;
-          const float *o = so + (iy * 9 + ix) * in_planes;
-          const float *wt = sw + ((ky * 3 + kx) * in_planes) * kC + n;
-          for (int c = 0; c < in_planes; ++c) acc = fmaf(o[c], wt[c * kC], acc);
+      if (binary) {
+        const uint8_t *mb = masks + eb * 128;
+#pragma unroll
+        for (int tap = 0; tap < 9; ++tap) {
+          const int m = mb[(y + tap / 3) * 11 + (xx + tap % 3)];
+          if (m == 0) continue;
+          const float *lt = sw + (tap * kStemSubsets + m) * kC + 4 * g;
+          const float4 l0 = *reinterpret_cast<const float4 *>(lt);
+          const float4 l1 = *reinterpret_cast<const float4 *>(lt + 64);
+          acc[0] += l0.x;
+          acc[1] += l0.y;
+          acc[2] += l0.z;
+          acc[3] += l0.w;
+          acc[4] += l1.x;
+          acc[5] += l1.y;
+          acc[6] += l1.z;
+          acc[7] += l1.w;
+        }
+      } else {
+        for (int ky = 0; ky < 3; ++ky) {
+          const int iy = y + ky - 1;
+          if (iy < 0 || iy >= 9) continue;
+          for (int kx = 0; kx < 3; ++kx) {
+            const int ix = xx + kx - 1;
+            if (ix < 0 || ix >= 9) continue;
+            const int tap = ky * 3 + kx;
+            const float *o = obs + ((size_t)(e0 + eb) * 81 + iy * 9 + ix) * in_planes;
+            for (int c = 0; c < in_planes; ++c) {
+              const float ov = o[c];
+              if (table) {
+                const float *wt = sw + (tap * kStemSubsets + (1 << c)) * kC + 4 * g;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = fmaf(ov, wt[(j >> 2) * 64 + (j & 3)], acc[j]);
+              } else {
+                const float *wt = sw + (tap * in_planes + c) * kC + n0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = fmaf(ov, wt[j], acc[j]);
+              }
+            }
+          }
         }
       }
     }
-    const size_t r = (size_t)e * kRowsPerBoard + p;
-    const T xb = F16Traits<T>::from_f(real ? acc : 0.0f);
-    x[r * kC + n] = xb;
-    const float av = fmaxf(fmaf(F16Traits<T>::to_f(xb), sc, sh), 0.0f);
-    a[r * kC + n] = F16Traits<T>::from_f(real ? av : 0.0f);
+    uint32_t px[4], pa[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      float xv[2], av[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const float xr = F16Traits<T>::to_f(F16Traits<T>::from_f(real ? acc[j + u] : 0.0f));
+        xv[u] = xr;
+        av[u] = real ? fmaxf(fmaf(xr, sc[j + u], sh[j + u]), 0.0f) : 0.0f;
+      }
+      px[j / 2] = F16Traits<T>::pack(xv[0], xv[1]);
+      pa[j / 2] = F16Traits<T>::pack(av[0], av[1]);
+    }
+    const size_t r = (size_t)(e0 + eb) * kRowsPerBoard + p;
+    *reinterpret_cast<uint4 *>(x + r * kC + n0) = make_uint4(px[0], px[1], px[2], px[3]);
+    *reinterpret_cast<uint4 *>(a + r * kC + n0) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
   }
 }
 
 // ---------------------------------------------------------------------------
-// heads: per board, the linears on the 1x1-conv features, then
-// dirichlet_from_logits (network.py:150-212, log-concentration heads)
+// heads: the linears on the 1x1-conv features, then dirichlet_from_logits
+// (network.py:150-212, log-concentration heads).  A CTA serves
+// kHeadBoards boards so every weight it reads feeds all of them; each
+// dot product keeps one fixed summation order.
 // ---------------------------------------------------------------------------
+
+constexpr int kHeadBoards = 16;
+constexpr int kFeat = 81 * kHeadCh;
 
 struct HeadWeights {
   int A;
@@ -580,80 +813,141 @@ struct HeadWeights {
   const float *qconc_w2, *qconc_b2;          // [128][A], [A]
 };
 
-__device__ __forceinline__ float block_sum128(float v, float *red) {
-  for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  return red[0] + red[1] + red[2] + red[3];
+size_t head_smem_bytes(int A) {
+  return (size_t)kHeadBoards * (kFeat + 3 * kC + 3 * A) * sizeof(float);
 }
 
-__global__ void __launch_bounds__(128) head_kernel(const float *feat, HeadWeights hw, float *logits,
+// sum over k < 128 of h[k] * w[k * stride]: lanes 32-wide butterflies per
+// 32-element block, blocks added in order
+__device__ __forceinline__ float warp_dot128(const float *h, const float *w, int stride, int lane) {
+  float total = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float v = h[j * 32 + lane] * w[(j * 32 + lane) * stride];
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    total = j == 0 ? v : total + v;
+  }
+  return total;
+}
+
+__global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards, HeadWeights hw, float *logits,
                                                    float *log_alpha_v, float *log_alpha_q, float *alpha_v,
                                                    float *alpha_q) {
-  __shared__ float f[81 * kHeadCh];
-  __shared__ float hv[kC], hq[kC], hc[kC];
-  __shared__ float mq[2 * 128], cq[128];
-  __shared__ float red[8];
-  const int e = blockIdx.x, t = threadIdx.x, A = hw.A;
-  for (int i = t; i < 81 * kHeadCh; i += 128) {
-    const int pos = i / kHeadCh, c = i % kHeadCh;
+  constexpr int G = kHeadBoards;
+  extern __shared__ float hs[];
+  const int A = hw.A, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float *f = hs;                 // [G][81 * 6]
+  float *hv = f + G * kFeat;     // [G][128]
+  float *hq = hv + G * kC;
+  float *hc = hq + G * kC;
+  float *mq = hc + G * kC;       // [G][2A]
+  float *cq = mq + G * 2 * A;    // [G][A]
+  const int e0 = blockIdx.x * G;
+  const int nb = min(G, boards - e0);
+  for (int i = t; i < G * kFeat; i += 128) {
+    const int g = i / kFeat, k = i % kFeat;
+    const int pos = k / kHeadCh, c = k % kHeadCh;
     const int y = pos / 9, x = pos % 9;
-    f[i] = feat[((size_t)e * kRowsPerBoard + (y + 1) * 10 + x) * 8 + c];
+    f[i] = g < nb ? feat[((size_t)(e0 + g) * kRowsPerBoard + (y + 1) * 10 + x) * 8 + c] : 0.0f;
   }
   __syncthreads();
   // policy logits: flatten (y, x, c) of the 2-channel policy features
   for (int a = t; a < A; a += 128) {
-    float acc = hw.policy_b[a];
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = hw.policy_b[a];
+#pragma unroll 4
     for (int pos = 0; pos < 81; ++pos)
-      for (int c = 0; c < 2; ++c) acc = fmaf(f[pos * kHeadCh + c], hw.policy_w[(pos * 2 + c) * A + a], acc);
-    logits[(size_t)e * A + a] = acc;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float wv = hw.policy_w[(pos * 2 + c) * A + a];
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] = fmaf(f[g * kFeat + pos * kHeadCh + c], wv, acc[g]);
+      }
+    for (int g = 0; g < nb; ++g) logits[(size_t)(e0 + g) * A + a] = acc[g];
   }
   // hidden layers (thread t = hidden unit t)
   {
-    float v = hw.value_b1[t], q = hw.qdir_b1[t], c = hw.qconc_b1[t];
-    for (int pos = 0; pos < 81; ++pos) {
-      v = fmaf(f[pos * kHeadCh + 2], hw.value_w1[pos * kC + t], v);
-      c = fmaf(f[pos * kHeadCh + 5], hw.qconc_w1[pos * kC + t], c);
-      q = fmaf(f[pos * kHeadCh + 3], hw.qdir_w1[(pos * 2) * kC + t], q);
-      q = fmaf(f[pos * kHeadCh + 4], hw.qdir_w1[(pos * 2 + 1) * kC + t], q);
+    float v[G], q[G], c[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      v[g] = hw.value_b1[t];
+      q[g] = hw.qdir_b1[t];
+      c[g] = hw.qconc_b1[t];
     }
-    hv[t] = fmaxf(v, 0.0f);
-    hq[t] = fmaxf(q, 0.0f);
-    hc[t] = fmaxf(c, 0.0f);
+#pragma unroll 4
+    for (int pos = 0; pos < 81; ++pos) {
+      const float wv = hw.value_w1[pos * kC + t], wc = hw.qconc_w1[pos * kC + t];
+      const float wq0 = hw.qdir_w1[(pos * 2) * kC + t], wq1 = hw.qdir_w1[(pos * 2 + 1) * kC + t];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float *fp = f + g * kFeat + pos * kHeadCh;
+        v[g] = fmaf(fp[2], wv, v[g]);
+        c[g] = fmaf(fp[5], wc, c[g]);
+        q[g] = fmaf(fp[3], wq0, q[g]);
+        q[g] = fmaf(fp[4], wq1, q[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      hv[g * kC + t] = fmaxf(v[g], 0.0f);
+      hq[g * kC + t] = fmaxf(q[g], 0.0f);
+      hc[g * kC + t] = fmaxf(c[g], 0.0f);
+    }
   }
   __syncthreads();
-  // value head: 2 mean logits + 1 log-concentration
-  const float m0 = block_sum128(hv[t] * hw.value_mean_w[t * 2], red) + hw.value_mean_b[0];
-  const float m1 = block_sum128(hv[t] * hw.value_mean_w[t * 2 + 1], red) + hw.value_mean_b[1];
-  const float cv = block_sum128(hv[t] * hw.value_conc_w[t], red) + hw.value_conc_b[0];
-  if (t == 0) {
-    const float cc = fminf(fmaxf(cv, -80.0f), 80.0f);
-    const float mx = fmaxf(m0, m1);
-    const float lse = mx + logf(expf(m0 - mx) + expf(m1 - mx));
-    log_alpha_v[e * 2] = cc + (m0 - lse);
-    log_alpha_v[e * 2 + 1] = cc + (m1 - lse);
-    alpha_v[e * 2] = expf(cc + (m0 - lse));
-    alpha_v[e * 2 + 1] = expf(cc + (m1 - lse));
+  // value head: 2 mean logits + 1 log-concentration, one warp per board
+  for (int g = warp; g < nb; g += 4) {
+    const float *h = hv + g * kC;
+    const float m0 = warp_dot128(h, hw.value_mean_w, 2, lane) + hw.value_mean_b[0];
+    const float m1 = warp_dot128(h, hw.value_mean_w + 1, 2, lane) + hw.value_mean_b[1];
+    const float cv = warp_dot128(h, hw.value_conc_w, 1, lane) + hw.value_conc_b[0];
+    if (lane == 0) {
+      const int e = e0 + g;
+      const float cc = fminf(fmaxf(cv, -80.0f), 80.0f);
+      const float mx = fmaxf(m0, m1);
+      const float lse = mx + logf(expf(m0 - mx) + expf(m1 - mx));
+      log_alpha_v[e * 2] = cc + (m0 - lse);
+      log_alpha_v[e * 2 + 1] = cc + (m1 - lse);
+      alpha_v[e * 2] = expf(cc + (m0 - lse));
+      alpha_v[e * 2 + 1] = expf(cc + (m1 - lse));
+    }
   }
   // Q heads
   for (int j = t; j < 2 * A; j += 128) {
-    float acc = hw.qdir_b2[j];
-    for (int k = 0; k < kC; ++k) acc = fmaf(hq[k], hw.qdir_w2[k * 2 * A + j], acc);
-    mq[j] = acc;
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = hw.qdir_b2[j];
+#pragma unroll 8
+    for (int k = 0; k < kC; ++k) {
+      const float wv = hw.qdir_w2[k * 2 * A + j];
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(hq[g * kC + k], wv, acc[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) mq[g * 2 * A + j] = acc[g];
   }
   for (int a = t; a < A; a += 128) {
-    float acc = hw.qconc_b2[a];
-    for (int k = 0; k < kC; ++k) acc = fmaf(hc[k], hw.qconc_w2[k * A + a], acc);
-    cq[a] = acc;
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = hw.qconc_b2[a];
+#pragma unroll 8
+    for (int k = 0; k < kC; ++k) {
+      const float wv = hw.qconc_w2[k * A + a];
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(hc[g * kC + k], wv, acc[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) cq[g * A + a] = acc[g];
   }
   __syncthreads();
-  for (int a = t; a < A; a += 128) {
-    const float cc = fminf(fmaxf(cq[a], -80.0f), 80.0f);
-    const float q0 = mq[2 * a], q1 = mq[2 * a + 1];
+  for (int i = t; i < nb * A; i += 128) {
+    const int g = i / A, a = i % A;
+    const float cc = fminf(fmaxf(cq[g * A + a], -80.0f), 80.0f);
+    const float q0 = mq[g * 2 * A + 2 * a], q1 = mq[g * 2 * A + 2 * a + 1];
     const float mx = fmaxf(q0, q1);
     const float lse = mx + logf(expf(q0 - mx) + expf(q1 - mx));
-    const size_t o = ((size_t)e * A + a) * 2;
+    const size_t o = ((size_t)(e0 + g) * A + a) * 2;
     log_alpha_q[o] = cc + (q0 - lse);
     log_alpha_q[o + 1] = cc + (q1 - lse);
     alpha_q[o] = expf(cc + (q0 - lse));
@@ -682,12 +976,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2D 16-bit tensor [rows, 128] with 64 x 128 boxes and 128-byte swizzle (the
 // copy is type-agnostic; the MMA's instruction descriptor names the format)
-bool make_map(CUtensorMap *map, const void *base, uint64_t rows) {
+bool make_map(CUtensorMap *map, const void *base, uint64_t rows, uint32_t box_rows = kBM) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)kC, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)kC * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -709,7 +1003,7 @@ template <typename T>
 int launch_conv(const void *in, const void *w, void *out0, void *out1, const EpiParams &ep, uint64_t rows_alloc,
                 cudaStream_t stream) {
   CUtensorMap m_in, m_w, m_o0, m_o1;
-  if (!make_map(&m_in, in, rows_alloc) || !make_map(&m_w, w, 9 * kC)) return SCACCHI_ECUDA;
+  if (!make_map(&m_in, in, rows_alloc, kWinBoxRows) || !make_map(&m_w, w, 9 * kC)) return SCACCHI_ECUDA;
   if (!make_map(&m_o0, out0 ? out0 : in, rows_alloc)) return SCACCHI_ECUDA;
   if (!make_map(&m_o1, out1 ? out1 : (out0 ? out0 : in), rows_alloc)) return SCACCHI_ECUDA;
   static bool attr = false;
@@ -718,7 +1012,8 @@ int launch_conv(const void *in, const void *w, void *out0, void *out1, const Epi
     attr = true;
   }
   const int tiles = (int)(rows_alloc / kBM);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int pairs = (tiles + 1) / 2;
+  const int grid = pairs < num_sms() ? pairs : num_sms();
   conv_tc_kernel<T><<<grid, kThreads, SmemLayout::kBytes, stream>>>(m_in, m_w, m_o0, m_o1, ep, tiles);
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaPeekAtLastError() == cudaSuccess ? SCACCHI_OK : SCACCHI_ECUDA;
@@ -789,14 +1084,22 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
     cudaMemsetAsync(x + used * kC, 0, (rows - used) * kC * 2, st);
     cudaMemsetAsync(a + used * kC, 0, (rows - used) * kC * 2, st);
   }
-  const size_t smem = (size_t)(81 * w->in_planes + 9 * w->in_planes * kC) * sizeof(float);
+  const size_t smem = stem_smem_bytes(w->in_planes);
+  const int stem_grid = (boards + kStemBoards - 1) / kStemBoards;
+  static std::atomic<size_t> stem_attr{0};
+  if (smem > 48 * 1024 && stem_attr.load() < smem) {
+    cudaFuncSetAttribute(stem_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(stem_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    stem_attr.store(smem);
+  }
   if (w->fp16)
-    stem_kernel<__half><<<boards, kC, smem, st>>>(obs, w->in_planes, w->stem_w, w->stem_b, w->bn_scale, w->bn_shift,
-                                                  reinterpret_cast<__half *>(x), reinterpret_cast<__half *>(a));
+    stem_kernel<__half><<<stem_grid, kStemThreads, smem, st>>>(obs, boards, w->in_planes, w->stem_w, w->stem_b,
+                                                               w->bn_scale, w->bn_shift, reinterpret_cast<__half *>(x),
+                                                               reinterpret_cast<__half *>(a));
   else
-    stem_kernel<__nv_bfloat16><<<boards, kC, smem, st>>>(obs, w->in_planes, w->stem_w, w->stem_b, w->bn_scale,
-                                                         w->bn_shift, reinterpret_cast<__nv_bfloat16 *>(x),
-                                                         reinterpret_cast<__nv_bfloat16 *>(a));
+    stem_kernel<__nv_bfloat16><<<stem_grid, kStemThreads, smem, st>>>(
+        obs, boards, w->in_planes, w->stem_w, w->stem_b, w->bn_scale, w->bn_shift,
+        reinterpret_cast<__nv_bfloat16 *>(x), reinterpret_cast<__nv_bfloat16 *>(a));
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   const size_t conv_elems = (size_t)9 * kC * kC;
   for (int blk = 0; blk < w->num_blocks; ++blk) {
@@ -829,7 +1132,14 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
   hw.qconc_b1 = w->qconc_b1;
   hw.qconc_w2 = w->qconc_w2;
   hw.qconc_b2 = w->qconc_b2;
-  head_kernel<<<boards, 128, 0, st>>>(feat, hw, logits, log_alpha_v, log_alpha_q, alpha_v, alpha_q);
+  const size_t head_smem = head_smem_bytes(hw.A);
+  static std::atomic<size_t> head_attr{0};
+  if (head_smem > 48 * 1024 && head_attr.load() < head_smem) {
+    cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)head_smem);
+    head_attr.store(head_smem);
+  }
+  head_kernel<<<(boards + kHeadBoards - 1) / kHeadBoards, 128, head_smem, st>>>(feat, boards, hw, logits, log_alpha_v,
+                                                                                log_alpha_q, alpha_v, alpha_q);
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaPeekAtLastError() == cudaSuccess ? SCACCHI_OK : SCACCHI_ECUDA;
 }
