@@ -173,6 +173,14 @@ def instrumented_step(game, state, key, cfg):
     return ms, sim_stats.cpu().tolist(), bwd_stats.cpu().tolist()
 
 
+# DRAM bytes (read + write) of one launch from ncu captures of this workload
+# (`--metrics`/`--set full`, dram__bytes_read.sum + dram__bytes_write.sum):
+# backward launch 65 of the warm-up step, and a conv1-mode tower convolution
+# of the 16384-board forward.
+BACKWARD_TRAFFIC_BYTES = 23646720 + 512
+CONV_TRAFFIC_BYTES = 419833088 + 372915968
+
+
 def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dict:
     A = ACTIONS
     row = A * (4 + 4 + 8 + 1 + 1)  # children, payload, alpha, outcome, invalid
@@ -186,8 +194,9 @@ def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dic
     achieved = bytes_per_launch / avg_s / 1e9 if avg_s > 0 else 0.0
     return {
         "bound": "hbm", "kernel": f"{dominant}_kernel", "achieved": round(achieved, 2), "peak": peak,
-        "unit": "GB/s", "frac": round(achieved / peak, 5), "traffic": None,
-        "peak_source": peak_kind,
+        "unit": "GB/s", "frac": round(achieved / peak, 5),
+        "traffic": BACKWARD_TRAFFIC_BYTES if dominant == "backward" else None,
+        "traffic_source": "ncu capture of one backward launch (simulation 64)", "peak_source": peak_kind,
         "algorithmic_bytes_per_launch": int(bytes_per_launch), "avg_launch_ms": round(ms[dominant] / SIMS, 5),
         "kernel_share": {k: round(v / total, 4) for k, v in ms.items()},
         "work": {"descent_nodes": sim_stats[0], "descent_prior_gathers": sim_stats[1],
@@ -264,7 +273,8 @@ def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
         "evals_per_s": round(TOWER_BOARDS / (ms / 1e3), 1),
         "tflops": round(TOWER_FLOP_PER_BOARD * TOWER_BOARDS / (ms / 1e3) / 1e12, 2),
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": round(conv_tflops, 2), "peak": peak,
-                     "unit": "TFLOP/s", "frac": round(conv_tflops / peak, 4), "traffic": None, "peak_source": kind,
+                     "unit": "TFLOP/s", "frac": round(conv_tflops / peak, 4), "traffic": CONV_TRAFFIC_BYTES,
+                     "traffic_source": "ncu capture of one conv1-mode launch, 16384 boards", "peak_source": kind,
                      "avg_launch_ms": round(conv_ms, 4),
                      "algorithmic_flop_per_launch": CONV_FLOP_PER_BOARD * TOWER_BOARDS,
                      "note": "algorithmic FLOPs count the 81 board cells; the kernel also multiplies the 19 "
