@@ -424,15 +424,11 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
     }
     c.joint[Q - 1] = 1.0f;
   }
-  // winner contributions per interval
-  run = 0.0f;
+  // winner contributions per interval (Z holds this action's zero-CDF flag)
   float prev_int = 0.0f;
   for (int k = 0; k < Q; ++k) {
     const float d = c.D[k * T + a];
-    if (k > 0) run = run + hstep * (c.D[(k - 1) * T + a] + d);
-    const float cd = run / safe;
-    const bool pos = cd > 0.0f;
-    const int zf = unres && !pos;
+    const int zf = c.Z[k * T + a];
     const float f = c.F[k * T + a];
     const float olp = ((int)c.zc[k] - zf) > 0 ? -SM_INF : c.flp[k] - f;
     const float integ = (d / safe) * sm_expf(olp);
