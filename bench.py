@@ -286,22 +286,45 @@ FULL_LANES = 8192
 FULL_SIMS = 256
 
 
-def full_step_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
-    """The full self-play search step on one GPU: Hex 9x9, 8192 lanes, 256
+POPULATION_SAMPLES = 64
+
+
+def population_config(sims: int):
+    from scacchi_b200.types import (DirichletThompsonSearchConfig, MonteCarloPosteriorUpdateConfig,
+                                    PosteriorUpdateConfig, PosteriorUpdateKind, RootPolicySupport)
+
+    return DirichletThompsonSearchConfig(
+        num_simulations=sims, max_depth=sims, root_policy_support=RootPolicySupport.search_evidence,
+        policy_target_temperature=1.0,
+        posterior_update=PosteriorUpdateConfig(
+            kind=PosteriorUpdateKind.monte_carlo,
+            monte_carlo=MonteCarloPosteriorUpdateConfig(kappa=KAPPA, policy_samples=POPULATION_SAMPLES,
+                                                        policy_sample_chunk_size=32)))
+
+
+def full_step_bench(steps: int, warmup: int, fp16: bool = False, population: bool = False, world: int = 1,
+                    rank: int = 0) -> dict:
+    """The full self-play search step: Hex 9x9, 8192 lanes per GPU, 256
     simulations (tree capacity 257), the 6x128 AZDirichletNet with the
     reference's random init (zero-initialised heads) evaluating every leaf
-    on the tcgen05 tower, prefix-CDF posterior (kappa 1, Monte Carlo
-    fallback with 8 samples), exact terminal certificates, roots after 0-20
-    uniform random legal moves.  One step = one make_search(...)(roots, key)
-    call: root evaluation, 256 x (descent, Hex step, tower, expand,
-    backward), root readout and target packing."""
+    on the tcgen05 tower, exact terminal certificates, roots after 0-20
+    uniform random legal moves.  The posterior estimator is the guarded
+    prefix-CDF (kappa 1, Monte Carlo fallback with 8 samples), or with
+    `population` the Thompson population of 64 samples per node.  One step =
+    one make_search(...)(roots, key) call per rank: root evaluation, 256 x
+    (descent, Hex step, tower, expand, backward), root readout and target
+    packing, then the all-gather of the root targets over NCCL when there
+    are several ranks (lanes shard by rank with per-rank keys)."""
     import torch
+    import torch.distributed as dist
 
     from scacchi_b200 import random as R
+    from scacchi_b200.distributed import LaneSharding, gather_targets
     from scacchi_b200.hex import HexGame
     from scacchi_b200.network import AZDirichletNet, init_params
     from scacchi_b200.play_search import make_evaluator, make_search
 
+    sharding = LaneSharding(world, rank)
     game = HexGame(9)
     net = AZDirichletNet(init_params(0, he_all_layers=False), fp16=fp16)
     evaluator = make_evaluator(net)
@@ -316,28 +339,48 @@ def full_step_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
         tower_ms.append((a, b))
         return out
 
-    cfg = search_config(FULL_SIMS)
+    cfg = population_config(FULL_SIMS) if population else search_config(FULL_SIMS)
     search = make_search(game, timed_evaluator, cfg)
-    state = game.random_roots(FULL_LANES, R.PRNGKey(0), 0, 20)
-    key = R.PRNGKey(1)
+    # every rank samples its own roots (fold the rank into the root key)
+    state = game.random_roots(FULL_LANES, R.fold_in(R.PRNGKey(0), rank), 0, 20)
+    key = sharding.device_key(R.PRNGKey(1))
+
+    def step():
+        return gather_targets(search(state, key), sharding)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
     for _ in range(warmup):
-        search(state, key)
+        step()
+    torch.cuda.synchronize()
+    barrier()
     torch.cuda.synchronize()
     tower_ms.clear()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
-        search(state, key)
+        step()
     e1.record(stream)
     torch.cuda.synchronize()
+    barrier()
     ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     t_tower = sum(a.elapsed_time(b) for a, b in tower_ms) / steps
+    lanes = FULL_LANES * world
+    estimator = (f"Thompson population, {POPULATION_SAMPLES} samples, kappa 1" if population else
+                 "prefix_cdf kappa 1 (Monte Carlo fallback 8 samples)")
     return {
-        "workload": "full search step: Hex 9x9, 8192 lanes x 256 simulations, AZDirichletNet 6x128 "
-                    "(reference random init) on the tcgen05 tower, prefix_cdf kappa 1, roots 0-20 random moves",
-        "lanes": FULL_LANES, "num_simulations": FULL_SIMS, "dtype": "fp16" if fp16 else "bf16",
-        "ms_per_step": round(ms, 2), "sims_per_s": round(FULL_LANES * FULL_SIMS / (ms / 1e3), 1),
-        "leaf_evals_per_s": round(FULL_LANES * (FULL_SIMS + 1) / (ms / 1e3), 1),
+        "workload": f"full search step: Hex 9x9, {FULL_LANES} lanes/GPU x {FULL_SIMS} simulations, AZDirichletNet "
+                    f"6x128 (reference random init) on the tcgen05 tower, {estimator}, roots 0-20 random moves",
+        "lanes": lanes, "lanes_per_gpu": FULL_LANES, "num_simulations": FULL_SIMS,
+        "dtype": "fp16" if fp16 else "bf16", "n_gpus": world,
+        "ms_per_step": round(ms, 2), "sims_per_s": round(lanes * FULL_SIMS / (ms / 1e3), 1),
+        "leaf_evals_per_s": round(lanes * (FULL_SIMS + 1) / (ms / 1e3), 1),
         "tower_share": round(t_tower / ms, 4),
         "tower_tflops": round(TOWER_FLOP_PER_BOARD * FULL_LANES * (FULL_SIMS + 1) / (t_tower / 1e3) / 1e12, 2),
         "steps": steps, "warmup": warmup,
@@ -412,9 +455,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="search", choices=["search", "tower", "full"],
+    ap.add_argument("--workload", default="search", choices=["search", "tower", "full", "population"],
                     help="search: the isolated search kernels (default); tower: the residual tower alone; "
-                         "full: the full Hex search step with the tower evaluating leaves")
+                         "full: the full Hex search step with the tower evaluating leaves (1 GPU); "
+                         "population: the full step with the 64-sample Thompson-population estimator, "
+                         "lane-sharded over the ranks")
     ap.add_argument("--fp16", action="store_true", help="tower: fp16 operands instead of bf16")
     ap.add_argument("--profile", action="store_true",
                     help="profiling mode: warmup steps + one device-resident step, no JSON line "
@@ -456,17 +501,28 @@ def main() -> None:
                                                      "(density 0.4), He-normal weights seed 0", "boards": TOWER_BOARDS},
                               "tflops": t["tflops"], "roofline": t["roofline"]}), flush=True)
         return
-    if args.workload == "full":
+    if args.workload in ("full", "population"):
+        population = args.workload == "population"
+        if world > 1 and not population:
+            if rank == 0:
+                print("--workload full runs on one GPU; use --workload population for several", file=sys.stderr)
+            return
+        if world > 1:
+            dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        with ClockSampler(local) as clocks:
+            f = full_step_bench(args.steps, args.warmup, args.fp16, population, world, rank)
         if rank == 0:
-            f = full_step_bench(args.steps, args.warmup, args.fp16)
-            print(json.dumps({"metric": METRIC, "value": f["sims_per_s"], "unit": "sims/s", "n_gpus": 1,
+            print(json.dumps({"metric": METRIC, "value": f["sims_per_s"], "unit": "sims/s", "n_gpus": world,
                               "steps": args.steps, "warmup": args.warmup, "ms_per_step": f["ms_per_step"],
                               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                               "dtype": f["dtype"], "data": "synthetic",
-                              "config": {"workload": f["workload"], "lanes": FULL_LANES,
-                                         "num_simulations": FULL_SIMS},
+                              "config": {"workload": f["workload"], "lanes": f["lanes"],
+                                         "lanes_per_gpu": FULL_LANES, "num_simulations": FULL_SIMS,
+                                         "parallelism": f"dp{world} (lane-sharded)"},
                               "leaf_evals_per_s": f["leaf_evals_per_s"], "tower_share": f["tower_share"],
-                              "tower_tflops": f["tower_tflops"]}), flush=True)
+                              "tower_tflops": f["tower_tflops"], "clocks": clocks.summary()}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
         return
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
@@ -588,6 +644,7 @@ def main() -> None:
         if world == 1:
             line["tower"] = tower_bench(5, 3)
             line["full_step"] = full_step_bench(3, 3)
+            line["population_step"] = full_step_bench(3, 3, population=True)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
