@@ -1647,9 +1647,13 @@ constexpr size_t kCtaSmemLimit = 160 * 1024;
 
 size_t prefix_smem(int half_width) { return (size_t)kWarpsPerBlock * 6 * (2 * half_width + 1) * sizeof(float); }
 
+// Dynamic shared memory above 48 KB needs an opt-in; the CTA-per-lane
+// kernels also ask for the largest shared-memory carveout, so their
+// residency is set by registers and shared memory, not by the L1 split.
 template <typename K>
 void allow_smem(K kernel, size_t bytes) {
   if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
 }
 
 #define SCACCHI_DISPATCH(A, ...)                          \
@@ -1707,6 +1711,7 @@ int scacchi_simulate(const scacchi_tree *tree, const uint32_t *simulate_key, int
   uint8_t *pe = T.E > 0 ? parent_embedding : nullptr;
   SCACCHI_DISPATCH(T.A, {
     const size_t smem = cta_smem_floats<NS>(1) * sizeof(float);
+    allow_smem(simulate_cta_kernel<NS>, smem);
     simulate_cta_kernel<NS><<<T.B, 32 * NS, smem, as_stream(stream)>>>(
         T, simulate_key, max_depth, parent, action, active, pe, reinterpret_cast<unsigned long long *>(stats));
   });

@@ -54,10 +54,8 @@ constexpr int kRowsPerBoard = 100;
 constexpr int kBM = 128;         // rows per accumulator tile
 constexpr int kBK = 64;          // channels per K block (128 bytes of 16-bit values)
 constexpr int kTileBytes = kBM * kBK * 2;  // 16 KB
-#ifndef SCACCHI_CONV_BSTAGES
-#define SCACCHI_CONV_BSTAGES 4
-#endif
-constexpr int kBStages = SCACCHI_CONV_BSTAGES;  // weight tiles in flight
+constexpr int kBStages = 4;      // weight tiles in flight when both staging tiles are in use
+constexpr int kMaxBStages = 8;   // ... and when the epilogue leaves staging space unused
 constexpr int kBTileBytes = kC * kBK * 2;  // 16 KB: 128 outputs x 64 inputs of one tap
 constexpr int kWinLead = 16;     // window rows above (and below) a tile pair: taps shift by <= 11
 constexpr int kWinRows = 2 * kBM + 2 * kWinLead;    // 288
@@ -298,15 +296,20 @@ struct EpiParams {
 struct SmemLayout {
   static constexpr int kWinOff = 0;                                    // 2 halves x 36 KB
   static constexpr int kBOff = kWinOff + 2 * kWinHalfBytes;
-  static constexpr int kOutOff = kBOff + kBStages * kBTileBytes;       // 2 outputs x 2 halves x 16 KB
-  static constexpr int kParamOff = kOutOff + 4 * kTileBytes;           // floats
+  // staging tiles right after the weight ring, second output first: a
+  // mode that leaves staging unused extends the ring into it (conv1 has one
+  // output, 6 stages; the heads have none, 8 stages)
+  static constexpr int kOut1Off = kBOff + kBStages * kBTileBytes;      // 2 halves x 16 KB
+  static constexpr int kOut0Off = kOut1Off + 2 * kTileBytes;           // 2 halves x 16 KB
+  static constexpr int kParamOff = kOut0Off + 2 * kTileBytes;          // floats
   static constexpr int kParamFloats = 3 * kC + kHeadCh * kC + 8;
   static constexpr int kHeadPartOff = kParamOff + kParamFloats * 4;  // [128 rows][kHeadCh] floats
   static constexpr int kBarOff = kHeadPartOff + kBM * kHeadCh * 4;
-  static constexpr int kNumBars = 2 + 2 + 2 * kBStages + 2 + 2;
+  static constexpr int kNumBars = 2 + 2 + 2 * kMaxBStages + 2 + 2;
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
 };
-static_assert(SmemLayout::kBOff % 1024 == 0 && SmemLayout::kOutOff % 1024 == 0, "swizzled tiles 1024-aligned");
+static_assert(SmemLayout::kBOff % 1024 == 0 && SmemLayout::kOut1Off % 1024 == 0, "swizzled tiles 1024-aligned");
+static_assert(kBTileBytes == kTileBytes, "weight stages and staging halves share a size");
 static_assert(SmemLayout::kBytes <= 227 * 1024, "shared memory budget");
 
 // One 128-row accumulator of a tile: bias / folded BatchNorm / ReLU /
@@ -418,8 +421,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   uint64_t *win_full = reinterpret_cast<uint64_t *>(smem + SmemLayout::kBarOff);
   uint64_t *win_empty = win_full + 2;
   uint64_t *b_full = win_empty + 2;
-  uint64_t *b_empty = b_full + kBStages;
-  uint64_t *acc_full = b_empty + kBStages;
+  uint64_t *b_empty = b_full + kMaxBStages;
+  uint64_t *acc_full = b_empty + kMaxBStages;
+  const int nbs = ep.mode == kEpiConv1 ? 6 : (ep.mode == kEpiHeads ? kMaxBStages : kBStages);
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -439,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       mbar_init(&win_full[h], 1);
       mbar_init(&win_empty[h], 1);
     }
-    for (int s = 0; s < kBStages; ++s) {
+    for (int s = 0; s < kMaxBStages; ++s) {
       mbar_init(&b_full[s], 1);
       mbar_init(&b_empty[s], 1);
     }
@@ -477,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             tma_load_2d(sb, &tm_w, &b_full[bstage], h * kBK, tap * kC);
             b_issued |= 1u << bstage;
             b_parity = (b_parity & ~(1u << bstage)) | (bphase << bstage);
-            if (++bstage == kBStages) {
+            if (++bstage == nbs) {
               bstage = 0;
               bphase ^= 1u;
             }
@@ -485,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         }
       }
       // every load issued into shared memory lands before the CTA may exit
-      for (int s = 0; s < kBStages; ++s)
+      for (int s = 0; s < nbs; ++s)
         if (b_issued >> s & 1u) mbar_drain(&b_full[s], b_parity >> s & 1u);
     }
   } else if (warp == kThreads / 32 - 1) {
@@ -551,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
               }
             }
             umma_commit(&b_empty[bstage]);
-            if (++bstage == kBStages) {
+            if (++bstage == nbs) {
               bstage = 0;
               bphase ^= 1u;
             }
@@ -571,8 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     const int quad = warp & 3;              // TMEM lanes this warp may access
     const int half = (warp - 2) >> 2;       // column half: warps 2-5 -> 0, 6-9 -> 1
     const int et = threadIdx.x - 64;        // 0..255
-    uint8_t *out0 = smem + SmemLayout::kOutOff;
-    uint8_t *out1 = out0 + 2 * kTileBytes;
+    uint8_t *out0 = smem + SmemLayout::kOut0Off;
+    uint8_t *out1 = smem + SmemLayout::kOut1Off;
     float *head_part = reinterpret_cast<float *>(smem + SmemLayout::kHeadPartOff);
     volatile int *go = abort_flag + 1;  // elected thread's verdict for the pair
     int slot = 0;
