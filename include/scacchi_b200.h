@@ -213,6 +213,27 @@ int scacchi_root_readout(int32_t batch, int32_t num_actions, const float *native
                          float tail_scale, float min_half_range, float max_half_range, float *policy_target,
                          uint8_t *accepted, void *stream);
 
+/* _dirichlet_commitment_policy (play_search.py:627-705): the root policy
+ * an action is committed from.  sampled_policy is posterior_best_policy
+ * (scacchi_posterior_best_policy) over the commitment support with the
+ * commitment key; a root with v_outcome != -1 takes the one-hot of
+ * search_action instead.  The support is _root_policy_support of the
+ * legal actions, positive_evidence ([B, A], actions with search visits)
+ * and q_outcome; numerical != 0 replaces the normalised native policy by
+ * the safe Q21 estimate (_numerical_policy_readout). */
+int scacchi_commitment_policy(int32_t batch, int32_t num_actions, const float *sampled_policy,
+                              const int32_t *search_action, const float *alpha, const int8_t *q_outcome,
+                              const int8_t *v_outcome, const uint8_t *legal, const uint8_t *positive_evidence,
+                              int32_t search_evidence_support, int32_t numerical, int32_t half_width,
+                              float tail_scale, float min_half_range, float max_half_range, float *policy,
+                              void *stream);
+
+/* posterior_best_action (kind 0) and posterior_sample_action (kind 1,
+ * power-temperature jax.random.categorical with key uint32[2]),
+ * dirichlet_q_search.py:79-116. */
+int scacchi_commit_action(int32_t kind, const uint32_t *key, const float *policy, const uint8_t *legal,
+                          int32_t batch, int32_t num_actions, float temperature, int32_t *action, void *stream);
+
 /* ---- synthetic game (isolated search-kernel workload) ----------------- */
 
 int scacchi_synthetic_root(const scacchi_synthetic_params *params, int32_t batch, float *prior_logits,

@@ -1340,3 +1340,86 @@ void or_root_readout(int B, int A, const float *native, const float *visit_count
     normalize_on_support(tgt, support, A, temperature, target + r);
   }
 }
+
+/* ------------------------------------------------------------------ */
+/* action commitment (play_search.py:627-705, dirichlet_q_search.py:79-116) */
+/* ------------------------------------------------------------------ */
+
+/* _dirichlet_commitment_policy for one batch: `sampled` is
+ * posterior_best_policy over the commitment support with the commitment
+ * key; a categorical root takes the one-hot of the search action; the
+ * native policy is normalised on the support, and with the numerical
+ * update the safe Q21 estimate replaces it (_numerical_policy_readout). */
+void or_commitment_policy(int B, int A, const float *sampled, const int32_t *search_action, const float *alpha,
+                          const int8_t *q_outcome, const int8_t *v_outcome, const uint8_t *legal,
+                          const uint8_t *evidence, int search_evidence, int numerical, const or_prefix_params *prm,
+                          float *policy) {
+  float nat[MAX_ACTIONS], est[MAX_ACTIONS], raw[MAX_ACTIONS], dli[MAX_ACTIONS];
+  uint8_t support[MAX_ACTIONS], inv[MAX_ACTIONS];
+  for (int b = 0; b < B; ++b) {
+    const size_t r = (size_t)b * A;
+    const int root_cat = v_outcome[b] != NO_OUTCOME;
+    int any_candidate = 0;
+    for (int a = 0; a < A; ++a) {
+      nat[a] = root_cat ? (a == search_action[b] ? 1.0f : 0.0f) : sampled[r + a];
+      int cand = legal[r + a] && (evidence[r + a] || q_outcome[r + a] != NO_OUTCOME);
+      support[a] = cand;
+      any_candidate |= cand;
+    }
+    if (!search_evidence || !any_candidate)
+      for (int a = 0; a < A; ++a) support[a] = legal[r + a];
+    int has_support = 0;
+    for (int a = 0; a < A; ++a) {
+      inv[a] = !support[a];
+      has_support |= support[a];
+    }
+    normalize_on_support(nat, support, A, 1.0f, policy + r);
+    if (!numerical) continue;
+    float mass, nerr, hr;
+    uint8_t finite, clipped;
+    int32_t fic;
+    or_prefix_out po = {est, raw, &mass, &nerr, &finite, &hr, &clipped, dli, &fic};
+    prefix_cdf_lane(alpha + 2 * r, inv, q_outcome + r, A, prm, &po, 0);
+    float derr = 0.0f;
+    int derr_nan = 0;
+    for (int a = 0; a < A; ++a) {
+      float v = fabsf(dli[a]);
+      if (sm_isnan(v)) derr_nan = 1;
+      if (v > derr) derr = v;
+    }
+    int unsafe = clipped || !finite || (!derr_nan && derr > 0.01f);
+    if (has_support && !root_cat && !unsafe)
+      for (int a = 0; a < A; ++a) policy[r + a] = est[a];
+  }
+}
+
+/* posterior_best_action (kind 0) / posterior_sample_action (kind 1):
+ * argmax of the masked policy, or jax.random.categorical(key, logits) =
+ * argmax(logits + gumbel) of logits = log(clip(p, 1e-8, 1)) / T on the
+ * legal actions with positive policy (all legal ones if none has); the
+ * Gumbel noise is -log(-log(uniform(key, [B, A], tiny, 1))). */
+void or_commit_action(int kind, uint32_t k0, uint32_t k1, const float *policy, const uint8_t *legal, int B, int A,
+                      float temperature, int32_t *action) {
+  float score[MAX_ACTIONS];
+  sk_key key = {k0, k1};
+  for (int b = 0; b < B; ++b) {
+    const size_t r = (size_t)b * A;
+    int any_pos = 0;
+    for (int a = 0; a < A; ++a) any_pos |= legal[r + a] && policy[r + a] > 0.0f;
+    for (int a = 0; a < A; ++a) {
+      const float p = policy[r + a];
+      if (kind == 0) {
+        score[a] = legal[r + a] ? p : -SM_INF;
+        continue;
+      }
+      const int eligible = any_pos ? (legal[r + a] && p > 0.0f) : legal[r + a];
+      float c = p > 1e-8f ? p : 1e-8f;
+      if (sm_isnan(p)) c = p;
+      c = c < 1.0f ? c : 1.0f;
+      const float logit = eligible ? sm_logf(c) / temperature : SM_FMIN;
+      const float u = sk_uniform(key, (uint64_t)b * A + a, SM_TINY, 1.0f);
+      score[a] = logit + (-sm_logf(-sm_logf(u)));
+    }
+    action[b] = nan_first_argmax(score, A);
+  }
+}

@@ -547,3 +547,37 @@ def root_readout(native, summary: dict, legal, *, search_evidence: bool, tempera
         _p(np.ascontiguousarray(legal, np.uint8)), C.c_int(1 if search_evidence else 0),
         C.c_float(temperature), C.byref(prm), C.c_float(0.01), _p(target), _p(accepted))
     return target, accepted.astype(bool)
+
+
+# --------------------------------------------------------------------------
+# action commitment
+# --------------------------------------------------------------------------
+
+def commitment_policy(sampled, search_action, alpha, q_outcome, v_outcome, legal, evidence, *,
+                      search_evidence: bool, numerical: bool, rule: Rule = Rule()) -> np.ndarray:
+    """play_search._dirichlet_commitment_policy for given sampled (Monte
+    Carlo) policies."""
+    sampled = np.ascontiguousarray(sampled, np.float32)
+    B, A = sampled.shape
+    out = np.zeros((B, A), np.float32)
+    prm = prefix_params(rule.half_width, rule.tail_scale, rule.min_half_range, rule.max_half_range)
+    lib().or_commitment_policy(
+        C.c_int(B), C.c_int(A), _p(sampled), _p(np.ascontiguousarray(search_action, np.int32)),
+        _p(np.ascontiguousarray(alpha, np.float32)), _p(np.ascontiguousarray(q_outcome, np.int8)),
+        _p(np.ascontiguousarray(v_outcome, np.int8)), _p(np.ascontiguousarray(legal, np.uint8)),
+        _p(np.ascontiguousarray(evidence, np.uint8)), C.c_int(int(search_evidence)), C.c_int(int(numerical)),
+        C.byref(prm), _p(out))
+    return out
+
+
+def commit_action(kind: str, key, policy, legal, temperature: float = 1.0) -> np.ndarray:
+    """posterior_best_action (kind "argmax") / posterior_sample_action
+    (kind "sample")."""
+    policy = np.ascontiguousarray(policy, np.float32)
+    B, A = policy.shape
+    out = np.zeros(B, np.int32)
+    k0, k1 = _key(key if key is not None else [0, 0])
+    lib().or_commit_action(C.c_int(0 if kind == "argmax" else 1), C.c_uint32(k0), C.c_uint32(k1), _p(policy),
+                           _p(np.ascontiguousarray(legal, np.uint8)), C.c_int(B), C.c_int(A),
+                           C.c_float(temperature), _p(out))
+    return out

@@ -76,6 +76,8 @@ SIGNATURES = {
     "scacchi_thompson_sample": [P, P, P, P, I32, I32, P, P],
     "scacchi_update_posterior": [P, C.POINTER(Context), I32, I32, C.POINTER(UpdateParams), P, P, P, P, P],
     "scacchi_root_readout": [I32, I32, P, P, P, P, P, P, P, I32, F32, I32, F32, F32, F32, P, P, P],
+    "scacchi_commitment_policy": [I32, I32, P, P, P, P, P, P, P, I32, I32, I32, F32, F32, F32, P, P],
+    "scacchi_commit_action": [I32, P, P, P, I32, I32, F32, P, P],
     "scacchi_synthetic_root": [C.POINTER(SyntheticParams), I32, P, P, P, P, P, P, P, P],
     "scacchi_synthetic_evaluate": [C.POINTER(SyntheticParams), I32, P, P, P, P, P, P, P, P],
     "scacchi_synthetic_recurrent": [C.POINTER(SyntheticParams), I32, P, P, P, P, P, P, P, P, P],

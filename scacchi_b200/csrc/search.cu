@@ -1516,6 +1516,140 @@ __global__ void __launch_bounds__(kThreads) root_readout_kernel(int B, int A, co
   if (lane == 0 && accepted_out) accepted_out[b] = accepted;
 }
 
+// _dirichlet_commitment_policy (play_search.py:627-705): the root policy an
+// action is committed from.  `sampled` is posterior_best_policy over the
+// commitment support (computed by the caller with the commitment key);
+// a categorical root takes the one-hot of the search action instead.  The
+// native policy is normalised on the support; with the numerical update
+// the Q21 estimate replaces it where it is safe (_numerical_policy_readout,
+// play_search.py:161-229).
+template <int NS>
+__global__ void __launch_bounds__(kThreads) commitment_kernel(int B, int A, const float *sampled,
+                                                              const int32_t *search_action, const float2 *alpha,
+                                                              const int8_t *q_out, const int8_t *v_out,
+                                                              const uint8_t *legal, const uint8_t *evidence,
+                                                              int search_evidence, int numerical, PrefixParams P,
+                                                              float *policy) {
+  const int b = warp_lane_index(), lane = threadIdx.x % kWarp;
+  const PrefixScratch sc = prefix_scratch(2 * P.h + 1);
+  if (b >= B) return;
+  const bool root_cat = v_out[b] != kNoOutcome;
+  const int solved = search_action[b];
+  bool lg[NS], support[NS], inv[NS];
+  float nat[NS], a0[NS], a1[NS];
+  int8_t qo[NS];
+  bool any_cand = false;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const int a = lane + kWarp * j;
+    const size_t i = (size_t)b * A + a;
+    lg[j] = support[j] = false;
+    nat[j] = 0.0f;
+    a0[j] = a1[j] = 1.0f;
+    qo[j] = kNoOutcome;
+    if (a >= A) continue;
+    lg[j] = legal[i] != 0;
+    qo[j] = q_out[i];
+    const float2 v = alpha[i];
+    a0[j] = v.x;
+    a1[j] = v.y;
+    nat[j] = root_cat ? (a == solved ? 1.0f : 0.0f) : sampled[i];
+    // _root_policy_support, play_search.py:232-252
+    support[j] = lg[j] && (evidence[i] != 0 || qo[j] != kNoOutcome);
+    any_cand |= support[j];
+  }
+  const bool has_candidate = __any_sync(kFull, any_cand);
+  bool any_support = false;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    if (!search_evidence || !has_candidate) support[j] = lg[j];
+    inv[j] = !support[j];
+    any_support |= support[j] && lane + kWarp * j < A;
+  }
+  const bool has_support = __any_sync(kFull, any_support);
+  float out[NS];
+  warp_normalize_on_support<NS>(nat, support, A, lane, 1.0f, out);
+  if (numerical) {
+    float est[NS], raw[NS], dli[NS];
+    PrefixLane L;
+    warp_prefix_cdf<NS>(a0, a1, inv, qo, A, lane, P, sc, est, raw, dli, L);
+    float derr = 0.0f;
+    bool dnan = false;
+#pragma unroll
+    for (int j = 0; j < NS; ++j) {
+      if (lane + kWarp * j >= A) continue;
+      const float v = fabsf(dli[j]);
+      dnan |= v != v;
+      if (v > derr) derr = v;
+    }
+    derr = warp_max_float(derr);
+    dnan = __any_sync(kFull, dnan);
+    const bool unsafe = L.clipped || !L.finite || (!dnan && derr > 0.01f);
+    if (has_support && !root_cat && !unsafe) {
+#pragma unroll
+      for (int j = 0; j < NS; ++j) out[j] = est[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const int a = lane + kWarp * j;
+    if (a < A) policy[(size_t)b * A + a] = out[j];
+  }
+}
+
+// posterior_best_action / posterior_sample_action
+// (dirichlet_q_search.py:79-116): kind 0 takes the masked argmax, kind 1
+// samples jax.random.categorical(key, logits) = argmax(logits + Gumbel
+// noise) of the power-temperature logits log(clip(p, 1e-8, 1)) / T over the
+// legal actions with positive policy (all legal actions if none has).
+template <int NS>
+__global__ void __launch_bounds__(kThreads) commit_action_kernel(int kind, const uint32_t *key_words,
+                                                                 const float *policy, const uint8_t *legal, int B,
+                                                                 int A, float temperature, int32_t *action) {
+  const int b = warp_lane_index(), lane = threadIdx.x % kWarp;
+  if (b >= B) return;
+  const sk_key key = kind == 1 ? sk_key{key_words[0], key_words[1]} : sk_key{0u, 0u};
+  float p[NS];
+  bool lg[NS], pos[NS];
+  bool any_pos = false;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const int a = lane + kWarp * j;
+    const size_t i = (size_t)b * A + a;
+    p[j] = a < A ? policy[i] : 0.0f;
+    lg[j] = a < A && legal[i] != 0;
+    pos[j] = lg[j] && p[j] > 0.0f;
+    any_pos |= pos[j];
+  }
+  any_pos = __any_sync(kFull, any_pos);
+  float bv = -SM_INF;
+  int bi = INT_MAX;
+#pragma unroll
+  for (int j = 0; j < NS; ++j) {
+    const int a = lane + kWarp * j;
+    if (a >= A) continue;
+    float score;
+    if (kind == 0) {
+      score = lg[j] ? p[j] : -SM_INF;
+    } else {
+      const bool eligible = any_pos ? pos[j] : lg[j];
+      float c = p[j] > 1e-8f ? p[j] : 1e-8f;
+      if (p[j] != p[j]) c = p[j];
+      c = c < 1.0f ? c : 1.0f;
+      const float logit = eligible ? sm_logf(c) / temperature : SM_FMIN;
+      // jax.random.gumbel: -log(-log(uniform(key, [B, A], tiny, 1)))
+      const float u = sk_uniform(key, (uint64_t)b * A + a, SM_TINY, 1.0f);
+      score = logit + (-sm_logf(-sm_logf(u)));
+    }
+    if (beats(score, a, bv, bi)) {
+      bv = score;
+      bi = a;
+    }
+  }
+  const int best = warp_argmax(bv, bi);
+  if (lane == 0) action[b] = best;
+}
+
 // ------------------------------------------------------------------------
 // synthetic game
 // ------------------------------------------------------------------------
@@ -1869,6 +2003,38 @@ int scacchi_root_readout(int32_t batch, int32_t num_actions, const float *native
         batch, num_actions, native_policy, visit_counts, reinterpret_cast<const float2 *>(alpha), q_outcome,
         q_distance, v_outcome, legal, search_evidence_support, temperature, P, policy_target, accepted);
   });
+  return launched();
+}
+
+int scacchi_commitment_policy(int32_t batch, int32_t num_actions, const float *sampled_policy,
+                              const int32_t *search_action, const float *alpha, const int8_t *q_outcome,
+                              const int8_t *v_outcome, const uint8_t *legal, const uint8_t *positive_evidence,
+                              int32_t search_evidence_support, int32_t numerical, int32_t half_width,
+                              float tail_scale, float min_half_range, float max_half_range, float *policy,
+                              void *stream) {
+  if (!sampled_policy || !search_action || !alpha || !q_outcome || !v_outcome || !legal || !positive_evidence ||
+      !policy || batch < 0 || num_actions < 1 || num_actions > 128 || half_width < 1 || half_width > kMaxHalfWidth)
+    return SCACCHI_EINVAL;
+  if (batch == 0) return SCACCHI_OK;
+  PrefixParams P{half_width, tail_scale, min_half_range, max_half_range};
+  const size_t smem = prefix_smem(half_width);
+  SCACCHI_DISPATCH(num_actions, {
+    allow_smem(commitment_kernel<NS>, smem);
+    commitment_kernel<NS><<<blocks_for(batch), kThreads, smem, as_stream(stream)>>>(
+        batch, num_actions, sampled_policy, search_action, reinterpret_cast<const float2 *>(alpha), q_outcome,
+        v_outcome, legal, positive_evidence, search_evidence_support, numerical, P, policy);
+  });
+  return launched();
+}
+
+int scacchi_commit_action(int32_t kind, const uint32_t *key, const float *policy, const uint8_t *legal,
+                          int32_t batch, int32_t num_actions, float temperature, int32_t *action, void *stream) {
+  if ((kind != 0 && kind != 1) || !policy || !legal || !action || batch < 0 || num_actions < 1 ||
+      num_actions > 128 || (kind == 1 && (!key || !(temperature > 0.0f) || !sm_isfinite(temperature))))
+    return SCACCHI_EINVAL;
+  if (batch == 0) return SCACCHI_OK;
+  SCACCHI_DISPATCH(num_actions, (commit_action_kernel<NS><<<blocks_for(batch), kThreads, 0, as_stream(stream)>>>(
+                                    kind, key, policy, legal, batch, num_actions, temperature, action)));
   return launched();
 }
 

@@ -27,9 +27,9 @@ from .dirichlet_mctx.outcomes import NO_OUTCOME, align_categorical_outcome, outc
 from .dirichlet_mctx.posterior_updates import (DEFAULT_POLICY_SAMPLE_CHUNK_SIZE, update_posterior,
                                                update_posterior_prefix_cdf)
 from .dirichlet_mctx.tree import ptr, stream_handle
-from .types import (DirichletThompsonSearchConfig, MonteCarloPosteriorUpdateConfig, NumericalPosteriorUpdateConfig,
-                    PosteriorUpdateKind, QActionSet, QPairReduction, QSupervisionConfig, RootPolicySupport,
-                    SearchConfig, SearchKind)
+from .types import (ActionCommitmentConfig, ActionCommitmentType, DirichletThompsonSearchConfig,
+                    MonteCarloPosteriorUpdateConfig, NumericalPosteriorUpdateConfig, PosteriorUpdateKind, QActionSet,
+                    QPairReduction, QSupervisionConfig, RootPolicySupport, SearchConfig, SearchKind)
 
 TARGET_PAD = 0
 TARGET_DIRICHLET = 1
@@ -279,3 +279,146 @@ def make_search(env, evaluator: Callable, search_cfg: SearchConfig | DirichletTh
                                              stats=stats)
 
     return search
+
+
+# --------------------------------------------------------------------------
+# action commitment (play_search.py:627-831, dirichlet_q_search.py:79-116)
+# --------------------------------------------------------------------------
+
+def _commit(kind: int, rng_key, policy: torch.Tensor, legal_action_mask: torch.Tensor, temperature: float):
+    from .dirichlet_mctx.action_selection import key_tensor
+
+    B, A = policy.shape
+    dev = policy.device
+    action = torch.empty((B,), dtype=torch.int32, device=dev)
+    key = key_tensor(rng_key, dev) if kind == 1 else None
+    # converted operands stay referenced until the launch: a temporary freed
+    # between two pointer grabs could hand its block to the next one
+    pol = policy.to(torch.float32).contiguous()
+    legal = legal_action_mask.to(torch.uint8).contiguous()
+    _lib.check(_lib.lib().scacchi_commit_action(kind, ptr(key), ptr(pol), ptr(legal), B, A, float(temperature),
+                                                ptr(action), stream_handle(dev)), "commit_action")
+    return action
+
+
+def posterior_best_action(policy_target: torch.Tensor, legal_action_mask: torch.Tensor) -> torch.Tensor:
+    """dirichlet_q_search.py:79-86: argmax of the policy over legal actions."""
+    return _commit(0, None, policy_target, legal_action_mask, 1.0)
+
+
+def posterior_sample_action(rng_key, policy_target: torch.Tensor, legal_action_mask: torch.Tensor,
+                            temperature: float = 1.0) -> torch.Tensor:
+    """dirichlet_q_search.py:89-116: sample from the power-temperature
+    transform of a root policy (jax.random.categorical on
+    log(clip(p, 1e-8, 1)) / temperature over the legal actions with positive
+    policy)."""
+    import math
+
+    if not math.isfinite(temperature) or temperature <= 0.0:
+        raise ValueError(f"posterior sample temperature must be finite and > 0; got {temperature}.")
+    return _commit(1, rng_key, policy_target, legal_action_mask, temperature)
+
+
+def dirichlet_commitment_policy(posterior: PosteriorTargets, legal_action_mask: torch.Tensor, rng_key,
+                                search_config: DirichletThompsonSearchConfig,
+                                selected_update: PosteriorUpdateKind | None) -> torch.Tensor:
+    """play_search.py:627-705: the root policy an action is committed from."""
+    from .dirichlet_mctx.action_selection import posterior_best_policy
+
+    prediction, metadata = posterior.prediction, posterior.metadata
+    alpha = _required_output(prediction.alpha_q, "alpha_q")
+    if (metadata is None or metadata.search_action is None or metadata.q_target_outcome is None
+            or metadata.v_target_outcome is None):
+        raise ValueError("Dirichlet action commitment requires root posterior metadata.")
+    update_config = search_config.posterior_update.select(selected_update)
+    samples, chunk = _posterior_policy_sampling_budget(update_config)
+    dev = alpha.device
+    legal = legal_action_mask.to(torch.bool)
+    evidence = (torch.zeros_like(legal) if metadata.q_positive_evidence_action is None
+                else metadata.q_positive_evidence_action.to(torch.bool))
+    search_evidence = search_config.root_policy_support == RootPolicySupport.search_evidence
+    candidate = legal & (evidence | (metadata.q_target_outcome != NO_OUTCOME))
+    support = torch.where(candidate.any(-1, keepdim=True), candidate, legal) if search_evidence else legal
+    # the full batch with the original key, as the reference samples it
+    sampled = posterior_best_policy(rng_key, alpha, ~support, samples, chunk_size=chunk,
+                                    categorical_outcome=metadata.q_target_outcome)
+    B, A = sampled.shape
+    numerical = isinstance(update_config, NumericalPosteriorUpdateConfig)
+    num = search_config.posterior_update.numerical
+    policy = torch.empty((B, A), dtype=torch.float32, device=dev)
+    # converted operands stay referenced until the launch (see _commit)
+    operands = (sampled.contiguous(), metadata.search_action.to(torch.int32).contiguous(), alpha.contiguous(),
+                metadata.q_target_outcome.to(torch.int8).contiguous(),
+                metadata.v_target_outcome.to(torch.int8).contiguous(), legal.to(torch.uint8).contiguous(),
+                evidence.to(torch.uint8).contiguous())
+    _lib.check(_lib.lib().scacchi_commitment_policy(
+        B, A, *[ptr(t) for t in operands], int(search_evidence), int(numerical), int(num.half_width),
+        float(num.tail_scale), float(num.min_half_range), float(num.max_half_range), ptr(policy),
+        stream_handle(dev)), "commitment_policy")
+    return policy
+
+
+def make_action_committer(config: ActionCommitmentConfig,
+                          dirichlet_search_config: DirichletThompsonSearchConfig | None = None) -> Callable:
+    """play_search.py:708-750."""
+    from . import random as srandom
+
+    def action_committer(posterior: PosteriorTargets, legal_action_mask: torch.Tensor, rng_key) -> torch.Tensor:
+        metadata = posterior.metadata
+        search_action = None if metadata is None else metadata.search_action
+        policy = posterior.prediction.policy
+        action_key = rng_key
+        if dirichlet_search_config is not None and config.kind != ActionCommitmentType.search_action:
+            policy_key, action_key = srandom.split(rng_key)
+            policy = dirichlet_commitment_policy(posterior, legal_action_mask, policy_key, dirichlet_search_config,
+                                                 config.posterior_update)
+        if config.kind == ActionCommitmentType.posterior_argmax:
+            return posterior_best_action(policy, legal_action_mask)
+        if config.kind == ActionCommitmentType.posterior_sample:
+            return posterior_sample_action(action_key, policy, legal_action_mask,
+                                           temperature=config.posterior_sample_temperature)
+        if config.kind == ActionCommitmentType.search_action:
+            if search_action is None:
+                raise ValueError("search_action commitment requires a backend action")
+            return search_action
+        raise ValueError(f"unknown action_commitment_type: {config.kind!r}")
+
+    return action_committer
+
+
+def commit_action(action_commitment_type: str, rng_key, policy: torch.Tensor, legal_action_mask: torch.Tensor,
+                  search_action: torch.Tensor | None = None, posterior_sample_temperature: float = 1.0):
+    """play_search.py:753-784: commit an already-computed policy."""
+    try:
+        kind = ActionCommitmentType(action_commitment_type)
+    except ValueError as error:
+        raise ValueError(f"unknown action_commitment_type: {action_commitment_type!r}") from error
+    posterior = PosteriorTargets(prediction=PosteriorPrediction(policy=policy),
+                                 metadata=TargetMetadata(search_action=search_action))
+    return make_action_committer(ActionCommitmentConfig(kind=kind,
+                                                        posterior_sample_temperature=posterior_sample_temperature))(
+        posterior, legal_action_mask, rng_key)
+
+
+class PlayerOutput(NamedTuple):
+    action: torch.Tensor
+    posterior: PosteriorTargets
+
+
+def make_search_player(env, model: Any, search_cfg: SearchConfig, action_commitment: ActionCommitmentConfig,
+                       q_supervision_config: QSupervisionConfig | None = None) -> Callable:
+    """play_search.py:799-831: search, then commit an action."""
+    from . import random as srandom
+
+    search = make_search(env, make_evaluator(model), search_cfg, q_supervision_config)
+    committer = make_action_committer(
+        action_commitment,
+        search_cfg.dirichlet_thompson if search_cfg.kind == SearchKind.dirichlet_thompson else None)
+
+    def player(env_state, rng_key) -> PlayerOutput:
+        search_key, action_key = srandom.split(rng_key)
+        posterior = search(env_state, search_key)
+        action = committer(posterior, env_state.legal_action_mask, action_key)
+        return PlayerOutput(action=action, posterior=posterior)
+
+    return player

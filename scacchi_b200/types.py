@@ -1,7 +1,7 @@
 """Search configuration (the search-step part of scacchi/types.py).
 
 Same field names, defaults and validation messages as the reference's
-dataclasses (types.py:170-345, 394-400).  Only the Dirichlet-Thompson search
+dataclasses (types.py:24-28, 170-345, 362-377, 394-400).  Only the Dirichlet-Thompson search
 runs on this backend; the policy and Gumbel search kinds are accepted as
 configuration but rejected by ``make_search``.
 """
@@ -11,6 +11,12 @@ from __future__ import annotations
 import math
 from dataclasses import dataclass, field
 from enum import StrEnum
+
+
+class ActionCommitmentType(StrEnum):
+    posterior_argmax = "posterior_argmax"
+    posterior_sample = "posterior_sample"
+    search_action = "search_action"
 
 
 class SearchKind(StrEnum):
@@ -160,3 +166,18 @@ class SearchConfig:
 class QSupervisionConfig:
     action_set: QActionSet = QActionSet.positive_search_evidence_or_solved
     reduction: QPairReduction = QPairReduction.mean_over_selected_state_action_pairs
+
+
+@dataclass
+class ActionCommitmentConfig:
+    """types.py:362-377 of the reference."""
+
+    kind: ActionCommitmentType = ActionCommitmentType.posterior_argmax
+    # None reuses the updater selected by Dirichlet Thompson search.
+    posterior_update: PosteriorUpdateKind | None = None
+    posterior_sample_temperature: float = 1.0
+
+    def __post_init__(self) -> None:
+        if not math.isfinite(self.posterior_sample_temperature) or self.posterior_sample_temperature <= 0.0:
+            raise ValueError("action_commitment.posterior_sample_temperature must be finite and > 0; got "
+                             f"{self.posterior_sample_temperature}.")
