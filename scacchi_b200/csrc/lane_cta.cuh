@@ -555,17 +555,23 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
 // Shared memory already limits the 3-warp instance to 6 CTAs per SM; a
 // register budget for 5 keeps the kernel free of spills (tighter budgets
 // spill 60-120 bytes per thread and measured no faster).
+// RULE is the update rule of the launch (0: Monte Carlo, 1: guarded
+// prefix-CDF); the Monte Carlo instance carries no quadrature code, so it
+// needs fewer registers and more lanes fit on an SM.
 #ifndef SCACCHI_BWD_MIN_BLOCKS
 #define SCACCHI_BWD_MIN_BLOCKS 5
 #endif
+#ifndef SCACCHI_BWD_MC_MIN_BLOCKS
+#define SCACCHI_BWD_MC_MIN_BLOCKS 8
+#endif
 
-template <int W>
-__global__ void __launch_bounds__(32 * W, SCACCHI_BWD_MIN_BLOCKS) backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent,
-                                                              const int32_t *sim_action, const uint8_t *sim_active,
-                                                              const float2 *step_value, const int32_t *step_tp,
-                                                              UpdateParams P, unsigned long long *stats) {
+template <int W, int RULE>
+__global__ void __launch_bounds__(32 * W, RULE == 1 ? SCACCHI_BWD_MIN_BLOCKS : SCACCHI_BWD_MC_MIN_BLOCKS)
+    backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent, const int32_t *sim_action,
+                        const uint8_t *sim_active, const float2 *step_value, const int32_t *step_tp, UpdateParams P,
+                        unsigned long long *stats) {
   const int b = blockIdx.x, a = threadIdx.x;
-  const Cta<W> c = cta_scratch<W>(P.rule == 1 ? 2 * P.prefix.h + 1 : 1);
+  const Cta<W> c = cta_scratch<W>(RULE == 1 ? 2 * P.prefix.h + 1 : 1);
   const int A = T.A;
   const bool present = a < A;
   bool active = sim_active[b] != 0;
@@ -643,12 +649,12 @@ __global__ void __launch_bounds__(32 * W, SCACCHI_BWD_MIN_BLOCKS) backward_cta_k
     // search policy: guarded prefix-CDF or Monte Carlo
     float policy = 0.0f;
     bool unsafe = false;
-    if (P.rule == 1) {
+    if (RULE == 1) {
       const PrefixResult1 pr = cta_prefix_guarded<W>(c, eff0, eff1, inv, eo, A, P.prefix, P.density_tol);
       policy = pr.policy;
       unsafe = pr.unsafe;
     }
-    if (P.rule != 1 || unsafe)
+    if (RULE != 1 || unsafe)
       policy = cta_mc_policy<W>(c, update_key, eff0, eff1, inv, eo, true, P.samples, A, b, T.B);
     // mix_value_prior, posterior_updates.py:40-63
     float in2[2] = {policy * cache0, policy * cache1}, w2[2];

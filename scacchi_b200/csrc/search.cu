@@ -1882,10 +1882,15 @@ int scacchi_backward(const scacchi_tree *tree, const uint32_t *backward_key, con
   SCACCHI_DISPATCH(T.A, {
     const size_t smem = cta_smem_floats<NS>(Q) * sizeof(float);
     if (smem <= kCtaSmemLimit) {
-      allow_smem(backward_cta_kernel<NS>, smem);
-      backward_cta_kernel<NS><<<T.B, 32 * NS, smem, as_stream(stream)>>>(
-          T, backward_key, parent, action, active, reinterpret_cast<const float2 *>(step_value), step_to_play, P,
-          reinterpret_cast<unsigned long long *>(stats));
+      auto launch = [&](auto kernel) {
+        allow_smem(kernel, smem);
+        kernel<<<T.B, 32 * NS, smem, as_stream(stream)>>>(T, backward_key, parent, action, active,
+                                                           reinterpret_cast<const float2 *>(step_value),
+                                                           step_to_play, P,
+                                                           reinterpret_cast<unsigned long long *>(stats));
+      };
+      if (P.rule == 1) launch(backward_cta_kernel<NS, 1>);
+      else launch(backward_cta_kernel<NS, 0>);
     } else {
       // very fine grids: the warp-per-lane kernel recomputes instead of
       // holding [Q][A] matrices in shared memory
