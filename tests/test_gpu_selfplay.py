@@ -67,3 +67,24 @@ def test_play_training_frames_replay_on_the_restatement(cuda):
                 nxt = H.init_state(size, O.split(reset_keys[b])[1])
             boards[b] = nxt
     assert games >= B  # 30 frames of 5x5 finish at least one game per lane
+    # loss input on the device frames (loss.py:164-357): value targets of a
+    # finished game alternate +-1 back from its winning move, and the value
+    # mask covers exactly the frames whose game ends inside the window
+    from scacchi_b200.loss_input import TrainingLossConfig, make_compute_input_for_lossfn
+
+    s = make_compute_input_for_lossfn(TrainingLossConfig(terminal_parent_targets=True))(data)
+    vt = s.value_tgt.cpu().numpy()
+    vm = s.value_mask.cpu().numpy()
+    for b in range(B):
+        last = np.nonzero(term[b])[0]
+        assert np.array_equal(vm[b], np.arange(T) <= last[-1])
+        sign = 1.0
+        for t in range(last[-1], -1, -1):
+            if term[b, t]:
+                sign = 1.0
+            assert vt[b, t] == sign
+            sign = -sign
+    assert s.value_tgt.is_cuda and s.policy_tgt.shape == (B, T, size * size + 1)
+    win = term & (reward > 0)
+    assert np.array_equal(s.policy_tgt.cpu().numpy()[win].argmax(-1), acts[win])
+    assert (s.v_target_outcome.cpu().numpy()[win] == 1).all()
