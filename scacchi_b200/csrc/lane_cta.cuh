@@ -1,4 +1,6 @@
-// One CTA per search lane, one action per thread (W = ceil(A / 32) warps).
+// One CTA per search lane, one action per thread (W = ceil(A / 32) warps);
+// the heavy per-(action, sample) and per-(action, grid point) cells of the
+// estimators are spread over all threads through a compacted action list.
 //
 // The descent and the bottom-up repair walk a lane's tree one node at a
 // time, so their latency per node bounds the whole launch: a few deep lanes
@@ -28,6 +30,10 @@ struct Cta {
   uint8_t *Z;         // [Qs][kT] zero-CDF flags
   DrawKeys *keys;     // [kKeyChunk] derived keys of a chunk of samples
   int *best;          // [kKeyChunk] argmax of each sample of a chunk
+  float4 *shape;      // [2][kT] Gamma constants of the compacted sampled actions
+  int *live;          // [kT] compacted list of the actions that carry work
+  float *ascale, *asafe;  // [kT] per-action density shift and normaliser
+  float *zint, *jinc;     // [Q] integrand of a non-unresolved action; joint increments
   int Q;
 };
 
@@ -38,15 +44,18 @@ __host__ __device__ constexpr int cta_rows(int Q) { return Q > 11 ? Q : 11; }
 
 template <int W>
 __host__ __device__ constexpr size_t cta_smem_floats(int Q) {
-  return (size_t)4 * Cta<W>::kT + 16 + 2 * W + kKeyChunk + (size_t)kKeyChunk * (sizeof(DrawKeys) / sizeof(float)) +
-         7 * (size_t)Q + 3 * (size_t)cta_rows(Q) * Cta<W>::kT + ((size_t)cta_rows(Q) * Cta<W>::kT + 3) / 4;
+  return (size_t)8 * Cta<W>::kT + (size_t)4 * Cta<W>::kT + 16 + 2 * W + kKeyChunk +
+         (size_t)kKeyChunk * (sizeof(DrawKeys) / sizeof(float)) + 3 * (size_t)Cta<W>::kT + 9 * (size_t)Q +
+         3 * (size_t)cta_rows(Q) * Cta<W>::kT + ((size_t)cta_rows(Q) * Cta<W>::kT + 3) / 4;
 }
 
 template <int W>
 __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   Cta<W> c;
   float *p = smem;
+  c.shape = reinterpret_cast<float4 *>(p);  // first: 16-byte aligned
+  p += 8 * Cta<W>::kT;
   c.red = p;
   p += 4 * Cta<W>::kT;
   c.bc = p;
@@ -66,7 +75,13 @@ __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
   c.joint = p + 4 * Q;
   c.score = p + 5 * Q;
   c.zc = p + 6 * Q;
-  p += 7 * Q;
+  c.zint = p + 7 * Q;
+  c.jinc = p + 8 * Q;
+  p += 9 * Q;
+  c.live = reinterpret_cast<int *>(p);
+  c.ascale = p + Cta<W>::kT;
+  c.asafe = p + 2 * Cta<W>::kT;
+  p += 3 * Cta<W>::kT;
   const size_t m = (size_t)cta_rows(Q) * Cta<W>::kT;
   c.D = p;
   c.F = p + m;
@@ -250,9 +265,34 @@ __device__ __forceinline__ float draw_utility(const DrawKeys &k, const GammaShap
   return binary_utility(lg0, lg1);
 }
 
-// posterior_best_policy (action_selection.py:146-194), one action per thread.
-// Each thread first draws its action's utility for every sample of a chunk
-// (independent work, no barrier), then warps take one sample's argmax each.
+// Lists the actions whose flag is set in c.live, in increasing order, and
+// returns how many there are; `slot` receives a flagged action's position.
+// Per-(action, sample) and per-(action, grid point) work is then spread over
+// all threads of the CTA by position in that list, so illegal and resolved
+// actions leave no thread idle.
+template <int W>
+__device__ __forceinline__ int cta_compact(const Cta<W> &c, bool flag, int &slot) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const unsigned m = __ballot_sync(kFull, flag);
+  if (lane == 0) c.pi[warp] = __popc(m);
+  __syncthreads();
+  int off = 0, n = 0;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const int cw = c.pi[w];
+    off += w < warp ? cw : 0;
+    n += cw;
+  }
+  slot = off + __popc(m & ((1u << lane) - 1u));
+  if (flag) c.live[slot] = t;
+  __syncthreads();
+  return n;
+}
+
+// posterior_best_policy (action_selection.py:146-194).  The utilities of a
+// chunk of samples are drawn cell by cell over (sample, sampled action),
+// every thread taking cells in turn; warps then take one sample's argmax
+// each, and each thread counts its own action's hits.
 template <int W>
 __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, bool invalid, int8_t cat,
                                bool use_cat, int S, int A, int b, int B) {
@@ -261,11 +301,13 @@ __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, 
   const bool present = a < A;
   const bool exact = present && !invalid && use_cat && cat != kNoOutcome;
   const bool sampled = present && !invalid && !exact;
-  const uint64_t base = (uint64_t)b * A * 2u + (uint64_t)a * 2u, stride = (uint64_t)B * A * 2u;
-  GammaShape g0 = gamma_shape(1.0f), g1 = g0;
+  const uint64_t lane_base = (uint64_t)b * A * 2u, stride = (uint64_t)B * A * 2u;
+  int slot;
+  const int ns = cta_compact<W>(c, sampled, slot);
   if (sampled) {
-    g0 = gamma_shape(a0);
-    g1 = gamma_shape(a1);
+    const GammaShape g0 = gamma_shape(a0), g1 = gamma_shape(a1);
+    c.shape[2 * slot] = make_float4(g0.alpha, g0.d, g0.c, g0.logd);
+    c.shape[2 * slot + 1] = make_float4(g1.alpha, g1.d, g1.c, g1.logd);
   }
   const float fixed = exact ? categorical_utility(cat) : -SM_INF;
   // one sample draws with `key` itself; more samples split(split(key)[0], S)
@@ -275,8 +317,16 @@ __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, 
   for (int s0 = 0; s0 < S; s0 += kKeyChunk) {
     const int n = S - s0 < kKeyChunk ? S - s0 : kKeyChunk;
     if (a < n) c.keys[a] = draw_keys(S == 1 ? key : sk_split(sample_key, (uint64_t)(s0 + a)));
+    if (!sampled)
+      for (int s = 0; s < n; ++s) U[s * T + a] = fixed;
     __syncthreads();
-    for (int s = 0; s < n; ++s) U[s * T + a] = sampled ? draw_utility(c.keys[s], g0, g1, base, stride) : fixed;
+    for (int i = a; i < n * ns; i += T) {
+      const int s = i / ns, slot = i - s * ns;
+      const int aa = c.live[slot];
+      const float4 p0 = c.shape[2 * slot], p1 = c.shape[2 * slot + 1];
+      const GammaShape g0 = {p0.x, p0.y, p0.z, p0.w}, g1 = {p1.x, p1.y, p1.z, p1.w};
+      U[s * T + aa] = draw_utility(c.keys[s], g0, g1, lane_base + (uint64_t)aa * 2u, stride);
+    }
     __syncthreads();
     for (int s = warp; s < n; s += W) {
       float bv = -SM_INF;
@@ -311,9 +361,14 @@ struct PrefixResult1 {
 };
 
 // binary_posterior_best_policy_prefix_quadrature (prefix_cdf.py:217-445) and
-// the guard of update_posterior_prefix_cdf (posterior_updates.py:282-290),
-// one action per thread.  Returns early with unsafe = true as soon as the
-// clipping or density guard fires.
+// the guard of update_posterior_prefix_cdf (posterior_updates.py:282-290).
+// Running sums over grid points (trapezoid integrals, the policy's sum over
+// intervals) are taken by each action's own thread in grid order; the
+// transcendental work per (unresolved action, grid point) cell is spread
+// over all threads by the compacted list of unresolved actions.  Each cell
+// evaluates exactly the expression of the per-action loop, so the result
+// does not depend on the mapping.  Returns early with unsafe = true as soon
+// as the clipping or density guard fires.
 template <int W>
 __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1, bool invalid, int8_t outc, int A,
                                             const PrefixParams &P, float tol) {
@@ -324,7 +379,8 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
   const bool legal = present && !invalid;
   const bool unres = legal && outc == kNoOutcome;
   const bool cwin = legal && outc == 1;
-  const int n_unres = __syncthreads_count(unres);
+  int slot;
+  const int n_unres = cta_compact<W>(c, unres, slot);
   const bool has_unres = n_unres > 0;
   const bool has_legal = __syncthreads_or(legal);
   const bool has_cw = __syncthreads_or(cwin);
@@ -356,28 +412,50 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
   }
   __syncthreads();
   const float hstep = 0.5f * (hr / fh);
-  // density normalisation of this action
-  const float w = unres ? (a1 > SM_TINY ? a1 : SM_TINY) : 1.0f;
-  const float l = unres ? (a0 > SM_TINY ? a0 : SM_TINY) : 1.0f;
-  const float bl = sm_betalnf(w, l);
-  float scale = -SM_INF;
+  const int cells = n_unres * Q;
+  // log-density of this action on the grid; a resolved or illegal action
+  // has density 0 everywhere (so zero CDF and no log-CDF contribution)
   bool nan = false;
-  for (int k = 0; k < Q; ++k) {
-    const float ld = ((w * c.lx[k] + l * c.l1mx[k]) - bl) + c.lj[k];
-    c.D[k * T + a] = ld;
-    nan |= ld != ld;
-    if (ld > scale) scale = ld;
+  if (unres) {
+    const float w = a1 > SM_TINY ? a1 : SM_TINY;
+    const float l = a0 > SM_TINY ? a0 : SM_TINY;
+    const float bl = sm_betalnf(w, l);
+    float scale = -SM_INF;
+    for (int k = 0; k < Q; ++k) {
+      const float ld = ((w * c.lx[k] + l * c.l1mx[k]) - bl) + c.lj[k];
+      c.D[k * T + a] = ld;
+      nan |= ld != ld;
+      if (ld > scale) scale = ld;
+    }
+    c.ascale[a] = nan ? SM_NAN : scale;
+  } else {
+    for (int k = 0; k < Q; ++k) {
+      c.D[k * T + a] = 0.0f;
+      c.F[k * T + a] = 0.0f;
+      c.X[k * T + a] = 0.0f;
+      c.Z[k * T + a] = 0;
+    }
   }
-  if (nan) scale = SM_NAN;
-  float run = 0.0f, prev = 0.0f;
-  for (int k = 0; k < Q; ++k) {
-    const float d = unres ? sm_expf(c.D[k * T + a] - scale) : 0.0f;
-    c.D[k * T + a] = d;
-    if (k > 0) run = run + hstep * (prev + d);
-    prev = d;
+  __syncthreads();
+  for (int i = a; i < cells; i += T) {
+    const int k = i / n_unres, aa = c.live[i - k * n_unres];
+    c.D[k * T + aa] = sm_expf(c.D[k * T + aa] - c.ascale[aa]);
   }
-  const float dli = unres ? scale + sm_logf(run) : 0.0f;
+  __syncthreads();
+  // trapezoid running integral (kept in F until the CDF pass)
+  float run = 0.0f;
+  if (unres) {
+    float prev = 0.0f;
+    for (int k = 0; k < Q; ++k) {
+      const float d = c.D[k * T + a];
+      if (k > 0) run = run + hstep * (prev + d);
+      prev = d;
+      c.F[k * T + a] = run;
+    }
+  }
+  const float dli = unres ? c.ascale[a] + sm_logf(run) : 0.0f;
   const float safe = run > 0.0f ? run : 1.0f;
+  c.asafe[a] = safe;
   // guards available now: non-finite log-integral or |log-integral| > tol
   const float adli = fabsf(dli);
   const bool dnan = __syncthreads_or(present && adli != adli);
@@ -387,20 +465,19 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
     r.unsafe = true;
     return r;
   }
-  // per grid point: leave-one-out products and the joint maximum CDF
-  run = 0.0f;
-  for (int k = 0; k < Q; ++k) {
-    const float d = c.D[k * T + a];
-    if (k > 0) run = run + hstep * (c.D[(k - 1) * T + a] + d);
-    const float cd = run / safe;
+  // per grid point: CDF, its log and the zero-CDF flag
+  for (int i = a; i < cells; i += T) {
+    const int k = i / n_unres, aa = c.live[i - k * n_unres];
+    const float cd = c.F[k * T + aa] / c.asafe[aa];
     const bool pos = cd > 0.0f;
     const float f = pos ? sm_logf(cd) : 0.0f;
     const float m = f < 0.0f ? f : 0.0f;
-    c.F[k * T + a] = f;
-    c.X[k * T + a] = unres ? (pos ? m : -SM_INF) : 0.0f;
-    c.Z[k * T + a] = (unres && !pos) ? 1 : 0;
+    c.F[k * T + aa] = f;
+    c.X[k * T + aa] = pos ? m : -SM_INF;
+    c.Z[k * T + aa] = pos ? 0 : 1;
   }
   __syncthreads();
+  // leave-one-out products and the joint maximum CDF
   for (int k = warp; k < Q; k += W) {
     const float flp = column_sum<W>(c.F + k * T, A, lane);
     const float lsum = column_sum<W>(c.X + k * T, A, lane);
@@ -424,19 +501,31 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
     }
     c.joint[Q - 1] = 1.0f;
   }
-  // winner contributions per interval (Z holds this action's zero-CDF flag)
-  float prev_int = 0.0f;
-  for (int k = 0; k < Q; ++k) {
-    const float d = c.D[k * T + a];
-    const int zf = c.Z[k * T + a];
-    const float f = c.F[k * T + a];
+  // winner integrand per (action, grid point); an action with zero density
+  // (d = 0, CDF 0, normaliser 1) has the same integrand at every point
+  for (int k = a; k < Q; k += T) {
+    const float olp = (int)c.zc[k] > 0 ? -SM_INF : c.flp[k] - 0.0f;
+    c.zint[k] = (0.0f / 1.0f) * sm_expf(olp);
+  }
+  for (int i = a; i < cells; i += T) {
+    const int k = i / n_unres, aa = c.live[i - k * n_unres];
+    const float d = c.D[k * T + aa];
+    const int zf = c.Z[k * T + aa];
+    const float f = c.F[k * T + aa];
     const float olp = ((int)c.zc[k] - zf) > 0 ? -SM_INF : c.flp[k] - f;
-    const float integ = (d / safe) * sm_expf(olp);
-    if (k > 0) {
-      const float cc = hstep * (prev_int + integ);
-      c.X[(k - 1) * T + a] = cc > 0.0f ? cc : (cc != cc ? cc : 0.0f);
-    }
-    prev_int = integ;
+    c.D[k * T + aa] = (d / c.asafe[aa]) * sm_expf(olp);
+  }
+  __syncthreads();
+  // interval contributions (trapezoid of the integrand), clamped at 0
+  for (int k = 1; k < Q; ++k) {
+    const float i0 = unres ? c.D[(k - 1) * T + a] : c.zint[k - 1];
+    const float i1 = unres ? c.D[k * T + a] : c.zint[k];
+    const float cc = hstep * (i0 + i1);
+    c.X[(k - 1) * T + a] = cc > 0.0f ? cc : (cc != cc ? cc : 0.0f);
+  }
+  for (int j = a; j < Q - 1; j += T) {
+    const float jinc = c.joint[j + 1] - c.joint[j];
+    c.jinc[j] = jinc > 0.0f ? jinc : (jinc != jinc ? jinc : 0.0f);
   }
   __syncthreads();
   for (int j = warp; j < Q - 1; j += W) {
@@ -444,15 +533,20 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
     if (lane == 0) c.score[j] = sc;
   }
   __syncthreads();
+  // allocate each interval's joint increment in proportion to the
+  // contributions (uniformly over unresolved actions if they sum to 0)
   const float uden = (float)(n_unres > 1 ? n_unres : 1);
-  float prob = 0.0f;
-  for (int j = 0; j < Q - 1; ++j) {
-    float jinc = c.joint[j + 1] - c.joint[j];
-    jinc = jinc > 0.0f ? jinc : (jinc != jinc ? jinc : 0.0f);
+  const int icells = n_unres * (Q - 1);
+  for (int i = a; i < icells; i += T) {
+    const int j = i / n_unres, aa = c.live[i - j * n_unres];
     const float sc = c.score[j];
-    const float wgt = sc > 0.0f ? c.X[j * T + a] / sc : (unres ? 1.0f : 0.0f) / uden;
-    prob = prob + wgt * jinc;
+    const float wgt = sc > 0.0f ? c.X[j * T + aa] / sc : 1.0f / uden;
+    c.D[j * T + aa] = wgt * c.jinc[j];
   }
+  __syncthreads();
+  float prob = 0.0f;
+  if (unres)
+    for (int j = 0; j < Q - 1; ++j) prob = prob + c.D[j * T + a];
   // _finalize_policy, prefix_cdf.py:121-183
   const int first_cw = cta_reduce_min<W>(c, cwin ? a : INT_MAX);
   const float cs = legal ? (float)outc : -SM_INF;
@@ -559,14 +653,14 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
 // prefix-CDF); the Monte Carlo instance carries no quadrature code, so it
 // needs fewer registers and more lanes fit on an SM.
 #ifndef SCACCHI_BWD_MIN_BLOCKS
-#define SCACCHI_BWD_MIN_BLOCKS 5
+#define SCACCHI_BWD_MIN_BLOCKS 6
 #endif
 #ifndef SCACCHI_BWD_MC_MIN_BLOCKS
 #define SCACCHI_BWD_MC_MIN_BLOCKS 8
 #endif
 
 template <int W, int RULE>
-__global__ void __launch_bounds__(32 * W, RULE == 1 ? SCACCHI_BWD_MIN_BLOCKS : SCACCHI_BWD_MC_MIN_BLOCKS)
+__global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_BLOCKS : 5) : SCACCHI_BWD_MC_MIN_BLOCKS)
     backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent, const int32_t *sim_action,
                         const uint8_t *sim_active, const float2 *step_value, const int32_t *step_tp, UpdateParams P,
                         unsigned long long *stats) {
