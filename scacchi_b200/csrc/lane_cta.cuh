@@ -37,10 +37,11 @@ struct Cta {
   int Q;
 };
 
-constexpr int kKeyChunk = 32;
+constexpr int kKeyChunk = 16;
 
-// matrix rows: enough for Q grid points and for a chunk of sample utilities
-__host__ __device__ constexpr int cta_rows(int Q) { return Q > 11 ? Q : 11; }
+// matrix rows: enough for Q grid points and, over D, F and X together, for
+// a chunk of sample utilities, their second variates and the redraw list
+__host__ __device__ constexpr int cta_rows(int Q) { return Q > kKeyChunk ? Q : kKeyChunk; }
 
 template <int W>
 __host__ __device__ constexpr size_t cta_smem_floats(int Q) {
@@ -289,6 +290,58 @@ __device__ __forceinline__ int cta_compact(const Cta<W> &c, bool flag, int &slot
   return n;
 }
 
+// Utilities U[s][action] of samples s < n of a chunk for the ns compacted
+// sampled actions (their Gamma constants in c.shape), in four passes over
+// cells so that the rare branches of the Marsaglia-Tsang draw do not hold
+// whole warps: (1) the first proposal of both variates of every cell;
+// (2) the full draw for the variates whose first proposal was rejected,
+// from a list; (3) the alpha < 1 augmentation for the (action, outcome)
+// pairs listed in `aug`; (4) the utility.  Each variate goes through exactly
+// the operations of log_gamma_draw, so the values equal a per-cell draw.
+template <int W>
+__device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, int na, uint64_t lane_base,
+                               uint64_t stride) {
+  constexpr int T = Cta<W>::kT;
+  const int a = threadIdx.x;
+  float *const L[2] = {c.D, c.D + kKeyChunk * T};  // [kKeyChunk][T] each; L[0] becomes U
+  uint16_t *redo = reinterpret_cast<uint16_t *>(c.D + 2 * kKeyChunk * T);  // 2 * kKeyChunk * T entries
+  for (int i = a; i < n * ns; i += T) {
+    const int s = i / ns, slot = i - s * ns;
+    const int aa = c.live[slot];
+    const uint64_t base = lane_base + (uint64_t)aa * 2u;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const float4 p = c.shape[2 * slot + g];
+      float v;
+      if (gamma_first(c.keys[s], base + g, p.y, p.z, p.w, v))
+        L[g][s * T + aa] = v;
+      else
+        redo[atomicAdd(&c.pi[0], 1)] = (uint16_t)((s << 8) | (slot << 1) | g);
+    }
+  }
+  __syncthreads();
+  const int nr = c.pi[0];
+  for (int e = a; e < nr; e += T) {
+    const int code = redo[e], s = code >> 8, slot = (code >> 1) & 127, g = code & 1;
+    const int aa = c.live[slot];
+    const float4 p = c.shape[2 * slot + g];
+    const GammaShape gs = {p.x, p.y, p.z, p.w};
+    L[g][s * T + aa] = log_gamma_core(c.keys[s], lane_base + (uint64_t)aa * 2u + g, stride, gs);
+  }
+  __syncthreads();
+  for (int i = a; i < n * na; i += T) {
+    const int s = i / na, code = aug[i - s * na], slot = code >> 1, g = code & 1;
+    const int aa = c.live[slot];
+    float &lg = L[g][s * T + aa];
+    lg = gamma_augment(c.keys[s], lane_base + (uint64_t)aa * 2u + g, c.shape[2 * slot + g].x, lg);
+  }
+  __syncthreads();
+  for (int i = a; i < n * ns; i += T) {
+    const int s = i / ns, aa = c.live[i - s * ns];
+    L[0][s * T + aa] = binary_utility(L[0][s * T + aa], L[1][s * T + aa]);
+  }
+}
+
 // posterior_best_policy (action_selection.py:146-194).  The utilities of a
 // chunk of samples are drawn cell by cell over (sample, sampled action),
 // every thread taking cells in turn; warps then take one sample's argmax
@@ -304,11 +357,20 @@ __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, 
   const uint64_t lane_base = (uint64_t)b * A * 2u, stride = (uint64_t)B * A * 2u;
   int slot;
   const int ns = cta_compact<W>(c, sampled, slot);
+  // Gamma constants by slot, and the list of (slot, outcome) variates whose
+  // concentration is below 1 (they take the augmentation)
+  int *aug = reinterpret_cast<int *>(c.red);  // up to 2 * T entries
+  if (a == 0) c.pi[0] = 0;
+  __syncthreads();
   if (sampled) {
     const GammaShape g0 = gamma_shape(a0), g1 = gamma_shape(a1);
     c.shape[2 * slot] = make_float4(g0.alpha, g0.d, g0.c, g0.logd);
     c.shape[2 * slot + 1] = make_float4(g1.alpha, g1.d, g1.c, g1.logd);
+    if (g0.alpha < 1.0f) aug[atomicAdd(&c.pi[0], 1)] = 2 * slot;
+    if (g1.alpha < 1.0f) aug[atomicAdd(&c.pi[0], 1)] = 2 * slot + 1;
   }
+  __syncthreads();
+  const int na = c.pi[0];
   const float fixed = exact ? categorical_utility(cat) : -SM_INF;
   // one sample draws with `key` itself; more samples split(split(key)[0], S)
   const sk_key sample_key = sk_split(key, 0);
@@ -316,17 +378,13 @@ __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, 
   float *U = c.D;  // [kKeyChunk][T]
   for (int s0 = 0; s0 < S; s0 += kKeyChunk) {
     const int n = S - s0 < kKeyChunk ? S - s0 : kKeyChunk;
+    __syncthreads();  // the previous chunk's (or the list's) counter reads are done
+    if (a == 0) c.pi[0] = 0;
     if (a < n) c.keys[a] = draw_keys(S == 1 ? key : sk_split(sample_key, (uint64_t)(s0 + a)));
     if (!sampled)
       for (int s = 0; s < n; ++s) U[s * T + a] = fixed;
     __syncthreads();
-    for (int i = a; i < n * ns; i += T) {
-      const int s = i / ns, slot = i - s * ns;
-      const int aa = c.live[slot];
-      const float4 p0 = c.shape[2 * slot], p1 = c.shape[2 * slot + 1];
-      const GammaShape g0 = {p0.x, p0.y, p0.z, p0.w}, g1 = {p1.x, p1.y, p1.z, p1.w};
-      U[s * T + aa] = draw_utility(c.keys[s], g0, g1, lane_base + (uint64_t)aa * 2u, stride);
-    }
+    cta_draw_chunk<W>(c, n, ns, aug, na, lane_base, stride);
     __syncthreads();
     for (int s = warp; s < n; s += W) {
       float bv = -SM_INF;

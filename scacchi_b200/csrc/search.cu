@@ -202,9 +202,10 @@ __device__ __forceinline__ GammaShape gamma_shape(float alpha_in) {
 #define SCACCHI_DRAW_INLINE
 #endif
 
-__device__ SCACCHI_DRAW_INLINE float log_gamma_draw(const DrawKeys k, uint64_t idx, uint64_t stride,
+// log d + log(chosen) of the draw: everything but the alpha < 1 augmentation
+__device__ SCACCHI_DRAW_INLINE float log_gamma_core(const DrawKeys k, uint64_t idx, uint64_t stride,
                                                     const GammaShape g) {
-  const float alpha = g.alpha, d = g.d, c = g.c;
+  const float d = g.d, c = g.c;
   float chosen = 0.0f;
   bool found = false;
   float z0 = 0.0f;
@@ -231,9 +232,35 @@ __device__ SCACCHI_DRAW_INLINE float log_gamma_draw(const DrawKeys k, uint64_t i
     fb = fb > floor_ ? fb : floor_;
     chosen = fb * (fb * fb);
   }
-  float lg = g.logd + sm_logf(chosen);
-  if (alpha < 1.0f) lg = lg + sm_logf(sk_uniform_tiny(k.augment, idx)) / alpha;
-  return lg;
+  return g.logd + sm_logf(chosen);
+}
+
+// the Gamma(alpha + 1) -> Gamma(alpha) augmentation, log U^(1/alpha)
+__device__ __forceinline__ float gamma_augment(const DrawKeys &k, uint64_t idx, float alpha, float lg) {
+  return lg + sm_logf(sk_uniform_tiny(k.augment, idx)) / alpha;
+}
+
+__device__ __forceinline__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride,
+                                                const GammaShape &g) {
+  const float lg = log_gamma_core(k, idx, stride, g);
+  return g.alpha < 1.0f ? gamma_augment(k, idx, g.alpha, lg) : lg;
+}
+
+// The first proposal of the draw alone (p = 0, counter idx).  Returns true
+// with v = log d + log(cube) when it is accepted, which is then exactly
+// log_gamma_core's value; otherwise log_gamma_core must be run.
+__device__ __forceinline__ bool gamma_first(const DrawKeys &k, uint64_t idx, float d, float c, float logd, float &v) {
+  const float z = sk_normal(k.normal, idx);
+  const float base = 1.0f + c * z;
+  if (!(base > 0.0f)) return false;
+  const float cube = base * (base * base);
+  const float u = sk_uniform_tiny(k.accept, idx);
+  const float z2 = z * z;
+  const float lc = sm_logf(cube);
+  bool accept = u < 1.0f - 0.0331f * (z2 * z2);
+  if (!accept) accept = sm_logf(u) < 0.5f * z2 + d * ((1.0f - cube) + lc);
+  v = logd + lc;
+  return accept;
 }
 
 __device__ __forceinline__ float log_gamma_draw(const DrawKeys &k, uint64_t idx, uint64_t stride, float alpha) {
