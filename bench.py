@@ -78,6 +78,10 @@ class ClockSampler:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            # nvidia-smi takes a moment to start: begin timing once it samples
+            deadline = time.time() + 3.0
+            while time.time() < deadline and os.path.getsize(self.path) == 0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -177,11 +181,14 @@ def instrumented_step(game, state, key, cfg):
 # (`--metrics`/`--set full`, dram__bytes_read.sum + dram__bytes_write.sum):
 # backward launch 65 of the warm-up step, and a conv1-mode tower convolution
 # of the 16384-board forward.
-BACKWARD_TRAFFIC_BYTES = 23646720 + 512
+BACKWARD_TRAFFIC_BYTES = 23662336 + 3840
+# smsp__inst_executed.sum over the 128 backward launches of one step of this
+# workload (ncu launch list, profiles/backward_cta_search4096x128.md)
+BACKWARD_WARP_INST_PER_STEP = 25896082646
 CONV_TRAFFIC_BYTES = 419833088 + 372915968
 
 
-def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dict:
+def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str, sm_count: int, sm_mhz: float) -> dict:
     A = ACTIONS
     row = A * (4 + 4 + 8 + 1 + 1)  # children, payload, alpha, outcome, invalid
     bwd_bytes = bwd_stats[0] * (row + 24 + A * 12 + 12) + bwd_stats[1] * 25
@@ -192,6 +199,10 @@ def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dic
     bytes_per_launch = per.get(dominant, 0) / SIMS
     avg_s = ms[dominant] / SIMS / 1e3
     achieved = bytes_per_launch / avg_s / 1e9 if avg_s > 0 else 0.0
+    # the resource the backward kernel is actually bound by: instruction
+    # issue (one warp instruction per scheduler per cycle, 4 per SM)
+    issue_peak = sm_count * 4 * sm_mhz / 1e3
+    issue = BACKWARD_WARP_INST_PER_STEP / (ms["backward"] / 1e3) / 1e9 if ms.get("backward") else 0.0
     return {
         "bound": "hbm", "kernel": f"{dominant}_kernel", "achieved": round(achieved, 2), "peak": peak,
         "unit": "GB/s", "frac": round(achieved / peak, 5),
@@ -202,8 +213,13 @@ def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str) -> dic
         "work": {"descent_nodes": sim_stats[0], "descent_prior_gathers": sim_stats[1],
                  "backward_nodes": bwd_stats[0], "backward_child_gathers": bwd_stats[1],
                  "mc_fallback_nodes": bwd_stats[2]},
+        "issue": {"bound": "issue", "kernel": "backward_kernel", "achieved": round(issue, 1), "peak": round(issue_peak, 1),
+                  "unit": "G warp-inst/s", "frac": round(issue / issue_peak, 4) if issue_peak else None,
+                  "inst_source": "ncu smsp__inst_executed.sum, backward launches of one step",
+                  "peak_source": "4 schedulers x SMs x sampled SM clock"},
         "note": "search kernels are ALU-bound (in-kernel threefry, Q21 transcendentals); the HBM fraction is "
-                "algorithmic bytes over measured copy bandwidth",
+                "algorithmic bytes over measured copy bandwidth, the issue fraction is warp instructions "
+                "over the schedulers' issue rate",
     }
 
 
@@ -451,7 +467,7 @@ def run_reference(args, world: int, rank: int) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -628,7 +644,9 @@ def main() -> None:
     # ---- per-kernel roofline (one instrumented, untimed step) --------------
     peak, peak_kind = read_peaks()
     ms, sim_stats, bwd_stats = instrumented_step(game, state, key, cfg)
-    roof = roofline(ms, sim_stats, bwd_stats, peak, peak_kind)
+    sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+    clock_summary = clocks.summary()
+    roof = roofline(ms, sim_stats, bwd_stats, peak, peak_kind, sm_count, clock_summary["sm_mhz"] or 1965.0)
     barrier()
 
     if rank == 0:
@@ -636,7 +654,7 @@ def main() -> None:
             "metric": METRIC, "value": round(value, 2), "unit": "sims/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": workload_config(world),
-            "leaf_evals_per_s": round(evals, 2), "clocks": clocks.summary(),
+            "leaf_evals_per_s": round(evals, 2), "clocks": clock_summary,
             "e2e": {"value": round(e2e_value, 2), "unit": "sims/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": int(launches), "roofline": roof,

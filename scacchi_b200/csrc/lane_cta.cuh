@@ -298,7 +298,9 @@ __device__ __forceinline__ int cta_compact(const Cta<W> &c, bool flag, int &slot
 // from a list; (3) the alpha < 1 augmentation for the (action, outcome)
 // pairs listed in `aug`; (4) the utility.  Each variate goes through exactly
 // the operations of log_gamma_draw, so the values equal a per-cell draw.
-template <int W>
+// GU unrolls the two variates of pass (1): 2 measured faster in the Monte
+// Carlo kernel, 1 (less code next to the quadrature) in the prefix-CDF one.
+template <int W, int GU>
 __device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, int na, uint64_t lane_base,
                                uint64_t stride) {
   constexpr int T = Cta<W>::kT;
@@ -309,7 +311,7 @@ __device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, i
     const int s = i / ns, slot = i - s * ns;
     const int aa = c.live[slot];
     const uint64_t base = lane_base + (uint64_t)aa * 2u;
-#pragma unroll
+#pragma unroll GU
     for (int g = 0; g < 2; ++g) {
       const float4 p = c.shape[2 * slot + g];
       float v;
@@ -346,7 +348,7 @@ __device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, i
 // chunk of samples are drawn cell by cell over (sample, sampled action),
 // every thread taking cells in turn; warps then take one sample's argmax
 // each, and each thread counts its own action's hits.
-template <int W>
+template <int W, int GU>
 __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, bool invalid, int8_t cat,
                                bool use_cat, int S, int A, int b, int B) {
   constexpr int T = Cta<W>::kT;
@@ -384,7 +386,7 @@ __device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, 
     if (!sampled)
       for (int s = 0; s < n; ++s) U[s * T + a] = fixed;
     __syncthreads();
-    cta_draw_chunk<W>(c, n, ns, aug, na, lane_base, stride);
+    cta_draw_chunk<W, GU>(c, n, ns, aug, na, lane_base, stride);
     __syncthreads();
     for (int s = warp; s < n; s += W) {
       float bv = -SM_INF;
@@ -704,9 +706,9 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
 }
 
 // backward (search.py:146-171) with the built-in rules, one CTA per lane.
-// Shared memory already limits the 3-warp instance to 6 CTAs per SM; a
-// register budget for 5 keeps the kernel free of spills (tighter budgets
-// spill 60-120 bytes per thread and measured no faster).
+// Shared memory limits the 3-warp prefix-CDF instance to 6 CTAs per SM and
+// its register budget matches (no spills); the 4-warp instance keeps a
+// budget for 5, since tighter ones spill.
 // RULE is the update rule of the launch (0: Monte Carlo, 1: guarded
 // prefix-CDF); the Monte Carlo instance carries no quadrature code, so it
 // needs fewer registers and more lanes fit on an SM.
@@ -807,7 +809,7 @@ __global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_B
       unsafe = pr.unsafe;
     }
     if (RULE != 1 || unsafe)
-      policy = cta_mc_policy<W>(c, update_key, eff0, eff1, inv, eo, true, P.samples, A, b, T.B);
+      policy = cta_mc_policy<W, RULE == 1 ? 1 : 2>(c, update_key, eff0, eff1, inv, eo, true, P.samples, A, b, T.B);
     // mix_value_prior, posterior_updates.py:40-63
     float in2[2] = {policy * cache0, policy * cache1}, w2[2];
     cta_sums<W, 2>(c, in2, w2, A);
