@@ -19,12 +19,13 @@ TREE_FIELDS = ("parents", "children_index", "node_to_play", "node_categorical_ou
                "invalid_actions")
 
 
-def run_cuda(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, native=True, lanes=None):
+def run_cuda(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, native=True, lanes=None,
+             **env):
     from scacchi_b200 import dirichlet_mctx as dm
     from scacchi_b200 import random as R
     from scacchi_b200.synthetic import SyntheticGame, SyntheticGameConfig
 
-    game = SyntheticGame(SyntheticGameConfig(seed=seed, terminal_prob=terminal_prob))
+    game = SyntheticGame(SyntheticGameConfig(seed=seed, terminal_prob=terminal_prob, **env))
     root = game.root(B)
     rule = (functools.partial(dm.update_posterior_prefix_cdf, kappa=kappa, fallback_policy_samples=samples)
             if prefix else functools.partial(dm.update_posterior, kappa=kappa, policy_samples=samples))
@@ -36,10 +37,10 @@ def run_cuda(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1
     return out, stats.cpu().numpy()
 
 
-def run_oracle(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, lanes=None):
+def run_oracle(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, lanes=None, **env):
     from oracle import oracle as O
 
-    env = O.synth_params(seed=seed, terminal_prob=terminal_prob)
+    env = O.synth_params(seed=seed, terminal_prob=terminal_prob, **env)
     return O.search_synthetic(env, B, O.PRNGKey(key_seed), N, O.Rule(prefix_cdf=prefix, kappa=kappa,
                                                                       samples=samples),
                               max_depth=N, policy_samples=samples, lanes=lanes)
@@ -63,6 +64,27 @@ def test_small_search_bit_exact(cuda, prefix, terminal_prob):
     compare(out, want)
     if prefix:
         assert stats[2] == want.unsafe_updates
+
+
+@pytest.mark.parametrize("num_actions", [20, 50, 120], ids=["one_warp", "two_warps", "four_warps"])
+@pytest.mark.parametrize("prefix", [True, False], ids=["prefix_cdf", "mc"])
+def test_action_counts_bit_exact(cuda, num_actions, prefix):
+    # every CTA width; low concentrations make most variates take the
+    # alpha < 1 augmentation and many first proposals fail
+    env = dict(num_actions=num_actions, logc_mean=-1.0, logc_std=1.5)
+    out, stats = run_cuda(24, 16, prefix, 0.05, seed=3, key_seed=4, **env)
+    want = run_oracle(24, 16, prefix, 0.05, seed=3, key_seed=4, **env)
+    compare(out, want)
+    if prefix:
+        assert stats[2] == want.unsafe_updates
+
+
+@pytest.mark.parametrize("samples", [17, 40])
+def test_population_chunks_bit_exact(cuda, samples):
+    # several sample chunks, the last one partial
+    out, _ = run_cuda(16, 12, False, 0.05, seed=6, key_seed=7, samples=samples)
+    want = run_oracle(16, 12, False, 0.05, seed=6, key_seed=7, samples=samples)
+    compare(out, want)
 
 
 def test_python_loop_matches_native_loop(cuda):
