@@ -22,16 +22,27 @@
 //   warp 10     TMA producer of the windows: half h of the next pair loads
 //               as soon as the MMAs finish reading half h of this one
 //   warp 1      TMEM allocator and MMA issuer (one thread):
-//               tcgen05.mma.cta_group::1.kind::f16, M = N = 128, K = 16,
-//               16-bit operands -> fp32 in TMEM; a tap's A matrix starts at
-//               window row 16 + 128 * sub + shift (any row: the swizzle
-//               phase follows the address); four 128-column
-//               accumulators, so a pair's epilogue overlaps the next pair
-//   warps 2-9   epilogue, two warps per TMEM lane quadrant (64 columns
-//               each): tcgen05.ld 32x32b, fused bias / folded BatchNorm /
-//               ReLU / residual / next block's BN-ReLU, bf16 into
-//               128B-swizzled shared memory, TMA store; the last layer
-//               instead computes the heads' 1x1 convolutions per row.
+//               tcgen05.mma.cta_group::1.kind::f16, K = 16, 16-bit
+//               operands -> fp32 in TMEM.  The residual layers run
+//               transposed: M = 128 output channels (A = the weight tile),
+//               N = 256 rows of the pair (B = the window from row 16 +
+//               shift; any row: the swizzle phase follows the address), so
+//               TMEM lane = channel and column = row, and a pair takes half
+//               the MMA instructions of two M = N = 128 products (the
+//               issue rate of those bounded the kernel).  The last layer
+//               keeps one row per TMEM lane (M = N = 128 per sub-tile) for
+//               its per-row head sums.  Two 256-column accumulators, so a
+//               pair's epilogue overlaps the next pair
+//   warps 2-9   epilogue, two warps per TMEM lane quadrant: fused bias /
+//               folded BatchNorm / ReLU / residual / next block's BN-ReLU,
+//               bf16 into 128B-swizzled shared memory, TMA store.
+//               Transposed layers read TMEM with tcgen05.ld 16x256b (the
+//               mma fragment layout) and transpose 8x8 blocks into the
+//               row-major staging tile with stmatrix .trans; the residual
+//               comes back the same way through ldmatrix .trans, and is
+//               prefetched into L2 a pair ahead.  The last layer reads
+//               32x32b (one row per thread) and computes the heads' 1x1
+//               convolutions per row.
 //
 // Every mbarrier wait is bounded: on timeout the kernel raises an error
 // flag, stops issuing, drains its own copies and releases TMEM.
@@ -156,7 +167,14 @@ __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk
 __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
+
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// bring `bytes` (a multiple of 16) of global memory at a 16-byte aligned
+// address into L2 ahead of use
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_barrier_init() {
@@ -207,6 +225,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 16 TMEM lanes x 8 columns in the mma fragment layout: thread t receives
+// lane t/4 columns 2(t%4), 2(t%4)+1 (r[0], r[1]) and lane t/4 + 8, same
+// columns (r[2], r[3]).  Asynchronous until tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// four 8x8 16-bit matrices between the fragment layout (thread t: row t/4,
+// columns 2(t%4), 2(t%4)+1 of matrix i in register i) and shared memory,
+// transposed: fragment column c is memory row c, whose 16-byte address
+// thread 8i + c supplies
+__device__ __forceinline__ void stmatrix_x4_trans(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
 }
 
 // shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
@@ -266,6 +310,14 @@ struct F16Traits<__half> {
 template <typename T>
 __host__ __device__ constexpr uint32_t idesc_for() {
   return (1u << 4) | (F16Traits<T>::kFormat << 7) | (F16Traits<T>::kFormat << 10) | ((128u >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+
+// the transposed product of the residual layers: M = 128 output channels
+// (A = a weight tile), N = 256 rows of a tile pair (B = the window)
+template <typename T>
+__host__ __device__ constexpr uint32_t idesc_tr() {
+  return (1u << 4) | (F16Traits<T>::kFormat << 7) | (F16Traits<T>::kFormat << 10) | ((256u >> 3) << 17) |
          ((128u >> 4) << 24);
 }
 
@@ -392,6 +444,92 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const float *
   }
 }
 
+__device__ __forceinline__ bool row_real(const EpiParams &ep, int r) {
+  const int p = r % kRowsPerBoard;
+  return r < ep.rows_valid && p >= 10 && (p % 10) != 9;
+}
+
+// The warp's 64 rows x 32 channels of the residual (conv2), global -> registers,
+// issued before the staging buffer frees so their latency overlaps the wait.
+template <typename T>
+__device__ __forceinline__ void load_residual_tr(const EpiParams &ep, int tile, int quad, int wh, int lane,
+                                                 uint4 (&res)[8]) {
+  const T *base = static_cast<const T *>(ep.residual) + ((size_t)tile * kBM + wh * 64) * kC + quad * 32;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int idx = k * 32 + lane;
+    res[k] = *reinterpret_cast<const uint4 *>(base + (size_t)(idx >> 2) * kC + (idx & 3) * 8);
+  }
+}
+
+// One 128-row tile of a transposed accumulator (TMEM lane = output channel,
+// column = row): bias / folded BatchNorm / ReLU / residual / next block's
+// BN-ReLU exactly as epilogue_tile, computed in the fragment layout of
+// tcgen05.ld 16x256b and written row-major into the 128B-swizzled staging
+// tile by stmatrix .trans.  The warp covers channels 32 * quad + [0, 32)
+// (its TMEM lane quadrant) and rows 64 * wh + [0, 64).  For conv2 the
+// residual is first stored into out0 where its sum will go and read back
+// in the fragment layout by ldmatrix .trans.  `cst` holds this thread's
+// bias, BN scale and BN shift of channels 32 * quad + 8 m + lane / 4.
+template <typename T>
+__device__ __forceinline__ void epilogue_tile_tr(const EpiParams &ep, const float (&cst)[3][4], uint32_t acc_addr,
+                                                 int tile, int quad, int wh, int lane, uint8_t *out0, uint8_t *out1,
+                                                 const uint4 (&res)[8]) {
+  const bool conv2 = ep.mode == kEpiConv2;
+  uint8_t *h0 = out0 + (quad >> 1) * kTileBytes;
+  uint8_t *h1 = out1 + (quad >> 1) * kTileBytes;
+  const int row_base = wh * 64, chunk0 = (quad & 1) * 4;
+  if (conv2) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int idx = k * 32 + lane;
+      *reinterpret_cast<uint4 *>(h0 + swz(row_base + (idx >> 2), chunk0 + (idx & 3))) = res[k];
+    }
+    __syncwarp();
+  }
+  const int mrow = lane & 7, mat = lane >> 3;
+  const uint32_t lane_addr = acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)row_base;
+#pragma unroll 1
+  for (int jj = 0; jj < 4; ++jj) {
+    uint32_t d[2][2][4];  // [block of the two][lane group][fragment register]
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2)
+#pragma unroll
+      for (int g = 0; g < 2; ++g) tmem_ld16x256(lane_addr + ((uint32_t)(16 * g) << 16) + 8 * (2 * jj + j2), d[j2][g]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2) {
+      const int rb = row_base + 8 * (2 * jj + j2);  // first row of the 8-row block in the tile
+      const int r0 = tile * kBM + rb + 2 * (lane & 3);
+      const bool real0 = row_real(ep, r0), real1 = row_real(ep, r0 + 1);
+      const int srow = rb + mrow, schunk = chunk0 + mat;
+      const uint32_t a0 = smem_u32(h0 + swz(srow, schunk));
+      uint32_t rv[4] = {0u, 0u, 0u, 0u};
+      if (conv2) ldmatrix_x4_trans(a0, rv);
+      uint32_t p0[4], p1[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int g = m >> 1, hi = m & 1;
+        const float y0 = __uint_as_float(d[j2][g][2 * hi]) + cst[0][m];
+        const float y1 = __uint_as_float(d[j2][g][2 * hi + 1]) + cst[0][m];
+        if (!conv2) {
+          p0[m] = F16Traits<T>::pack(real0 ? fmaxf(y0, 0.0f) : 0.0f, real1 ? fmaxf(y1, 0.0f) : 0.0f);
+        } else {
+          const T *rh = reinterpret_cast<const T *>(&rv[m]);
+          const float x0 = F16Traits<T>::to_f(F16Traits<T>::from_f(y0 + F16Traits<T>::to_f(rh[0])));
+          const float x1 = F16Traits<T>::to_f(F16Traits<T>::from_f(y1 + F16Traits<T>::to_f(rh[1])));
+          const float b0 = fmaxf(fmaf(x0, cst[1][m], cst[2][m]), 0.0f);
+          const float b1 = fmaxf(fmaf(x1, cst[1][m], cst[2][m]), 0.0f);
+          p0[m] = F16Traits<T>::pack(real0 ? x0 : 0.0f, real1 ? x1 : 0.0f);
+          p1[m] = F16Traits<T>::pack(real0 ? b0 : 0.0f, real1 ? b1 : 0.0f);
+        }
+      }
+      stmatrix_x4_trans(a0, p0);
+      if (conv2) stmatrix_x4_trans(smem_u32(h1 + swz(srow, schunk)), p1);
+    }
+  }
+}
+
 // heads: the row's two column halves' partial sums, bias, ReLU
 __device__ __forceinline__ void store_heads(const EpiParams &ep, const float *prm, int tile, int row_in_tile,
                                             const float (&lo)[kHeadCh], const float *hi) {
@@ -424,6 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   uint64_t *b_empty = b_full + kMaxBStages;
   uint64_t *acc_full = b_empty + kMaxBStages;
   const int nbs = ep.mode == kEpiConv1 ? 6 : (ep.mode == kEpiHeads ? kMaxBStages : kBStages);
+  // the residual layers run transposed (TMEM lane = output channel, column =
+  // row, half the MMA instructions); the heads keep one row per TMEM lane
+  const bool tr = ep.mode != kEpiHeads;
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -544,14 +685,23 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
             tc_fence_after();
             const uint32_t sb = smem_u32(smem + SmemLayout::kBOff + bstage * kBTileBytes);
             const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
+            if (tr) {
+              // D[channel][row] of both sub-tiles: one N = 256 product per K step
+              const uint32_t wrow = win + (uint32_t)(kWinLead + off) * 128u;
 #pragma unroll
-            for (int sub = 0; sub < 2; ++sub) {
-              const int w = kWinLead + sub * kBM + off;  // window row of the sub-tile's row 0
+              for (int k = 0; k < kBK / 16; ++k)
+                umma_f16(d0, smem_desc_sw128(sb + k * 32), smem_desc_sw128(wrow + k * 32), idesc_tr<T>(),
+                         (h | tap | k) != 0);
+            } else {
 #pragma unroll
-              for (int k = 0; k < kBK / 16; ++k) {
-                const uint64_t adesc = smem_desc_sw128(win + (uint32_t)w * 128u + k * 32);
-                const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
-                umma_f16(d0 + (uint32_t)(sub * kC), adesc, bdesc, idesc_for<T>(), (h | tap | k) != 0);
+              for (int sub = 0; sub < 2; ++sub) {
+                const int w = kWinLead + sub * kBM + off;  // window row of the sub-tile's row 0
+#pragma unroll
+                for (int k = 0; k < kBK / 16; ++k) {
+                  const uint64_t adesc = smem_desc_sw128(win + (uint32_t)w * 128u + k * 32);
+                  const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
+                  umma_f16(d0 + (uint32_t)(sub * kC), adesc, bdesc, idesc_for<T>(), (h | tap | k) != 0);
+                }
               }
             }
             umma_commit(&b_empty[bstage]);
@@ -581,7 +731,27 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     volatile int *go = abort_flag + 1;  // elected thread's verdict for the pair
     int slot = 0;
     uint32_t acc_phase = 0;
+    float cst[3][4];  // transposed epilogue: bias, BN scale, BN shift of this thread's channels
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int ch = quad * 32 + 8 * m + lane / 4;
+      cst[0][m] = prm[ch];
+      cst[1][m] = prm[kC + ch];
+      cst[2][m] = prm[2 * kC + ch];
+    }
+    // the residual of a pair is read by the epilogue only: prefetch it into
+    // L2 one pair ahead so its loads do not wait on HBM
+    const bool has_res = ep.mode != kEpiConv1;
+    auto prefetch_residual = [&](int p) {
+      for (int sub = 0; sub < 2; ++sub) {
+        const int tile = p * 2 + sub;
+        if (p < num_pairs && tile < num_tiles)
+          prefetch_l2(static_cast<const T *>(ep.residual) + (size_t)tile * kBM * kC, kBM * kC * (uint32_t)sizeof(T));
+      }
+    };
+    if (has_res && et == 0) prefetch_residual(blockIdx.x);
     for (int pair = blockIdx.x; pair < num_pairs; pair += gridDim.x) {
+      if (has_res && et == 0) prefetch_residual(pair + gridDim.x);
       // one thread waits (bounded) and broadcasts, so the epilogue threads agree
       if (et == 0) {
         const bool ok = !*abort_flag && mbar_wait(&acc_full[slot], acc_phase, abort_flag);
@@ -594,14 +764,20 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       for (int sub = 0; sub < 2; ++sub) {
         const int tile = pair * 2 + sub;
         if (tile >= num_tiles) break;  // uniform across the epilogue threads
+        uint4 res[8];
+        if (tr && ep.mode == kEpiConv2) load_residual_tr<T>(ep, tile, quad, half, lane, res);
         if (ep.mode != kEpiHeads) {
           // the staging buffers are free once the previous store has read them
           if (et == 0) tma_store_wait_read();
           asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
         }
         float head[kHeadCh];
-        epilogue_tile<T>(ep, prm, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0, out1,
-                         head);
+        if (tr)
+          epilogue_tile_tr<T>(ep, cst, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0,
+                              out1, res);
+        else
+          epilogue_tile<T>(ep, prm, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0,
+                           out1, head);
         if (ep.mode == kEpiHeads) {
           const int row_in_tile = quad * 32 + lane;
           if (half == 1) {
