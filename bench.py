@@ -185,7 +185,7 @@ BACKWARD_TRAFFIC_BYTES = 23662336 + 3840
 # smsp__inst_executed.sum over the 128 backward launches of one step of this
 # workload (ncu launch list, profiles/backward_cta_search4096x128.md)
 BACKWARD_WARP_INST_PER_STEP = 25896082646
-CONV_TRAFFIC_BYTES = 419833088 + 372915968
+CONV_TRAFFIC_BYTES = 420069888 + 370689536
 
 
 def roofline(ms: dict, sim_stats, bwd_stats, peak: float, peak_kind: str, sm_count: int, sm_mhz: float) -> dict:
