@@ -266,28 +266,104 @@ __device__ __forceinline__ float draw_utility(const DrawKeys &k, const GammaShap
   return binary_utility(lg0, lg1);
 }
 
-// Lists the actions whose flag is set in c.live, in increasing order, and
-// returns how many there are; `slot` receives a flagged action's position.
-// Per-(action, sample) and per-(action, grid point) work is then spread over
-// all threads of the CTA by position in that list, so illegal and resolved
-// actions leave no thread idle.
+// Two CTA-wide ORs and a float maximum (as cta_max_float) behind one barrier.
 template <int W>
-__device__ __forceinline__ int cta_compact(const Cta<W> &c, bool flag, int &slot) {
+__device__ __forceinline__ float cta_guards(const Cta<W> &c, bool f1, bool f2, float v, bool &any1, bool &any2) {
   const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
-  const unsigned m = __ballot_sync(kFull, flag);
-  if (lane == 0) c.pi[warp] = __popc(m);
+  const unsigned b1 = __ballot_sync(kFull, f1), b2 = __ballot_sync(kFull, f2);
+  const float m = warp_max_float(v);
+  if (lane == 0) {
+    c.pi[warp] = (b1 != 0u ? 1 : 0) | (b2 != 0u ? 2 : 0);
+    c.pv[warp] = m;
+  }
   __syncthreads();
-  int off = 0, n = 0;
+  int f = 0;
+  float r = c.pv[0];
 #pragma unroll
   for (int w = 0; w < W; ++w) {
-    const int cw = c.pi[w];
-    off += w < warp ? cw : 0;
-    n += cw;
+    f |= c.pi[w];
+    if (w > 0) r = c.pv[w] > r ? c.pv[w] : r;
   }
-  slot = off + __popc(m & ((1u << lane) - 1u));
-  if (flag) c.live[slot] = t;
   __syncthreads();
-  return n;
+  any1 = (f & 1) != 0;
+  any2 = (f & 2) != 0;
+  return r;
+}
+
+// Everything a node update reduces over its actions that is known once the
+// actions are gathered, in one pass: per-warp ballots and warp reductions,
+// one barrier, then every thread combines the W warps' partials.  The
+// results are integers, flags and an exact minimum, identical to separate
+// CTA reductions.  It also lists the unresolved legal actions in c.live in
+// increasing order: the estimators spread their per-(action, grid point)
+// and per-(action, sample) cells over all threads by position in that list,
+// so illegal and resolved actions leave no thread idle.
+struct NodeSummary {
+  int n_unres;       // unresolved legal actions (the length of c.live)
+  int slot;          // this thread's position in c.live, if it is listed
+  int delta;         // sum of the payload changes of the unresolved legal actions
+  bool has_legal, has_win;
+  int shortest_win;  // min payload over certified wins (INT_MAX if none)
+  int longest_loss;  // max payload over certified losses (INT_MIN if none)
+  int first_win;     // lowest certified winning action (INT_MAX if none)
+  float amin;        // min over unresolved of min(max(alpha, tiny)) per outcome
+  int visited;       // actions with a visited child (statistics only)
+};
+
+template <int W>
+__device__ __forceinline__ NodeSummary cta_node_summary(const Cta<W> &c, bool legal, bool unres, bool win, bool loss,
+                                                        int delta, int payload, float amin, bool visited) {
+  const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
+  const unsigned mu = __ballot_sync(kFull, unres), ml = __ballot_sync(kFull, legal);
+  const unsigned mw = __ballot_sync(kFull, win), mv = __ballot_sync(kFull, visited);
+  const int d = __reduce_add_sync(kFull, delta);
+  const int sw = __reduce_min_sync(kFull, win ? payload : INT_MAX);
+  const int ll = __reduce_max_sync(kFull, loss ? payload : INT_MIN);
+  const int fw = __reduce_min_sync(kFull, win ? t : INT_MAX);
+  const float am = warp_min_float(amin);
+  int *wi = reinterpret_cast<int *>(c.red);  // [W][8], then [W] floats
+  float *wf = c.red + 8 * W;
+  if (lane == 0) {
+    wi[warp * 8 + 0] = __popc(mu);
+    wi[warp * 8 + 1] = ml != 0u;
+    wi[warp * 8 + 2] = mw != 0u;
+    wi[warp * 8 + 3] = d;
+    wi[warp * 8 + 4] = sw;
+    wi[warp * 8 + 5] = ll;
+    wi[warp * 8 + 6] = fw;
+    wi[warp * 8 + 7] = __popc(mv);
+    wf[warp] = am;
+  }
+  __syncthreads();
+  NodeSummary r;
+  r.n_unres = 0;
+  r.delta = 0;
+  r.has_legal = false;
+  r.has_win = false;
+  r.shortest_win = INT_MAX;
+  r.longest_loss = INT_MIN;
+  r.first_win = INT_MAX;
+  r.amin = wf[0];
+  r.visited = 0;
+  int off = 0;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const int *q = wi + w * 8;
+    off += w < warp ? q[0] : 0;
+    r.n_unres += q[0];
+    r.has_legal |= q[1] != 0;
+    r.has_win |= q[2] != 0;
+    r.delta += q[3];
+    r.shortest_win = q[4] < r.shortest_win ? q[4] : r.shortest_win;
+    r.longest_loss = q[5] > r.longest_loss ? q[5] : r.longest_loss;
+    r.first_win = q[6] < r.first_win ? q[6] : r.first_win;
+    r.visited += q[7];
+    if (w > 0) r.amin = wf[w] < r.amin ? wf[w] : r.amin;
+  }
+  r.slot = off + __popc(mu & ((1u << lane) - 1u));
+  if (unres) c.live[r.slot] = t;
+  __syncthreads();
+  return r;
 }
 
 // Utilities U[s][action] of samples s < n of a chunk for the ns compacted
@@ -348,17 +424,18 @@ __device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, i
 // chunk of samples are drawn cell by cell over (sample, sampled action),
 // every thread taking cells in turn; warps then take one sample's argmax
 // each, and each thread counts its own action's hits.
+// Categorical edges take their exact utility, so the sampled actions are
+// exactly the node's unresolved legal ones: the summary's c.live list.
 template <int W, int GU>
-__device__ float cta_mc_policy(const Cta<W> &c, sk_key key, float a0, float a1, bool invalid, int8_t cat,
-                               bool use_cat, int S, int A, int b, int B) {
+__device__ float cta_mc_policy(const Cta<W> &c, const NodeSummary &sum, sk_key key, float a0, float a1, bool invalid,
+                               int8_t cat, int S, int A, int b, int B) {
   constexpr int T = Cta<W>::kT;
   const int a = threadIdx.x, lane = a % kWarp, warp = a / kWarp;
   const bool present = a < A;
-  const bool exact = present && !invalid && use_cat && cat != kNoOutcome;
+  const bool exact = present && !invalid && cat != kNoOutcome;
   const bool sampled = present && !invalid && !exact;
   const uint64_t lane_base = (uint64_t)b * A * 2u, stride = (uint64_t)B * A * 2u;
-  int slot;
-  const int ns = cta_compact<W>(c, sampled, slot);
+  const int slot = sum.slot, ns = sum.n_unres;
   // Gamma constants by slot, and the list of (slot, outcome) variates whose
   // concentration is below 1 (they take the augmentation)
   int *aug = reinterpret_cast<int *>(c.red);  // up to 2 * T entries
@@ -430,27 +507,19 @@ struct PrefixResult1 {
 // does not depend on the mapping.  Returns early with unsafe = true as soon
 // as the clipping or density guard fires.
 template <int W>
-__device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1, bool invalid, int8_t outc, int A,
-                                            const PrefixParams &P, float tol) {
+__device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &sum, float a0, float a1, bool invalid,
+                                            int8_t outc, int A, const PrefixParams &P, float tol) {
   const int a = threadIdx.x, lane = a % kWarp, warp = a / kWarp;
   const int h = P.h, Q = 2 * h + 1;
   const int T = Cta<W>::kT;
   const bool present = a < A;
   const bool legal = present && !invalid;
   const bool unres = legal && outc == kNoOutcome;
-  const bool cwin = legal && outc == 1;
-  int slot;
-  const int n_unres = cta_compact<W>(c, unres, slot);
+  const int n_unres = sum.n_unres;
   const bool has_unres = n_unres > 0;
-  const bool has_legal = __syncthreads_or(legal);
-  const bool has_cw = __syncthreads_or(cwin);
-  float amin = SM_INF;
-  if (unres) {
-    const float v0 = a0 > SM_TINY ? a0 : SM_TINY;
-    const float v1 = a1 > SM_TINY ? a1 : SM_TINY;
-    amin = v0 < v1 ? v0 : v1;
-  }
-  amin = cta_min_float<W>(c, amin);
+  const bool has_legal = sum.has_legal;
+  const bool has_cw = sum.has_win;
+  const float amin = sum.amin;
   float requested = sm_asinhf_pos(P.tail / amin);
   if (!has_unres) requested = P.min_hr;
   float hr = requested;
@@ -518,9 +587,9 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
   c.asafe[a] = safe;
   // guards available now: non-finite log-integral or |log-integral| > tol
   const float adli = fabsf(dli);
-  const bool dnan = __syncthreads_or(present && adli != adli);
-  const bool dinf = __syncthreads_or(unres && !sm_isfinite(dli));
-  const float derr = cta_max_float<W>(c, present ? adli : 0.0f);
+  bool dnan, dinf;
+  const float derr = cta_guards<W>(c, present && adli != adli, unres && !sm_isfinite(dli), present ? adli : 0.0f,
+                                   dnan, dinf);
   if (dinf || (!dnan && derr > tol)) {
     r.unsafe = true;
     return r;
@@ -608,7 +677,7 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, float a0, float a1,
   if (unres)
     for (int j = 0; j < Q - 1; ++j) prob = prob + c.D[j * T + a];
   // _finalize_policy, prefix_cdf.py:121-183
-  const int first_cw = cta_reduce_min<W>(c, cwin ? a : INT_MAX);
+  const int first_cw = sum.first_win;
   const float cs = legal ? (float)outc : -SM_INF;
   const int cbest = has_cw ? first_cw : cta_argmax_by_action<W>(c, cs, A);
   float raw = (has_cw || !has_unres) ? (a == cbest ? 1.0f : 0.0f) : (unres ? prob : 0.0f);
@@ -798,18 +867,26 @@ __global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_B
       cache0 = s * (eo == 0 ? 1.0f : 0.0f);
       cache1 = s * (eo == 1 ? 1.0f : 0.0f);
     }
-    const int delta = cta_reduce_add<W>(c, (present && unresolved && !inv) ? nep - ep : 0);
-    const int n_down = node_payload + delta;
+    const bool legal = present && !inv, unres = legal && unresolved;
+    float amin = SM_INF;
+    if (unres) {
+      const float v0 = eff0 > SM_TINY ? eff0 : SM_TINY;
+      const float v1 = eff1 > SM_TINY ? eff1 : SM_TINY;
+      amin = v0 < v1 ? v0 : v1;
+    }
+    const NodeSummary sum = cta_node_summary<W>(c, legal, unres, legal && eo == 1, legal && eo == 0,
+                                                unres ? nep - ep : 0, ep, amin, present && cvis);
+    const int n_down = node_payload + sum.delta;
     // search policy: guarded prefix-CDF or Monte Carlo
     float policy = 0.0f;
     bool unsafe = false;
     if (RULE == 1) {
-      const PrefixResult1 pr = cta_prefix_guarded<W>(c, eff0, eff1, inv, eo, A, P.prefix, P.density_tol);
+      const PrefixResult1 pr = cta_prefix_guarded<W>(c, sum, eff0, eff1, inv, eo, A, P.prefix, P.density_tol);
       policy = pr.policy;
       unsafe = pr.unsafe;
     }
     if (RULE != 1 || unsafe)
-      policy = cta_mc_policy<W, RULE == 1 ? 1 : 2>(c, update_key, eff0, eff1, inv, eo, true, P.samples, A, b, T.B);
+      policy = cta_mc_policy<W, RULE == 1 ? 1 : 2>(c, sum, update_key, eff0, eff1, inv, eo, P.samples, A, b, T.B);
     // mix_value_prior, posterior_updates.py:40-63
     float in2[2] = {policy * cache0, policy * cache1}, w2[2];
     cta_sums<W, 2>(c, in2, w2, A);
@@ -833,12 +910,11 @@ __global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_B
       T.edge_alpha[e] = make_float2(e0, e1);
     }
     // _categorize_node_and_publish (utils.py:67-124), binary outcomes
-    const bool known = present && !inv && !unresolved;
-    const bool has_legal = __syncthreads_or(present && !inv);
-    const bool any_open = __syncthreads_or(present && !inv && unresolved);
-    const bool has_win = __syncthreads_or(known && eo == 1);
-    const int shortest_win = cta_reduce_min<W>(c, (known && eo == 1) ? ep : INT_MAX);
-    const int longest_loss = cta_reduce_max<W>(c, (known && eo == 0) ? ep : INT_MIN);
+    const bool has_legal = sum.has_legal;
+    const bool any_open = sum.n_unres > 0;
+    const bool has_win = sum.has_win;
+    const int shortest_win = sum.shortest_win;
+    const int longest_loss = sum.longest_loss;
     const bool all_cat = has_legal && !any_open;
     const int8_t candidate = has_win ? 1 : (all_cat ? 0 : kNoOutcome);
     const int cdist = has_win ? shortest_win : longest_loss;
@@ -873,7 +949,7 @@ __global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_B
     }
     unsafe_n += unsafe;
     nodes += 1;
-    if (stats) child_gathers += (unsigned long long)cta_reduce_add<W>(c, present && cvis);
+    child_gathers += (unsigned long long)sum.visited;
     __syncthreads();
     const bool up = node != 0;
     const int parent = T.parents[ni];
