@@ -181,10 +181,10 @@ def instrumented_step(game, state, key, cfg):
 # (`--metrics`/`--set full`, dram__bytes_read.sum + dram__bytes_write.sum):
 # backward launch 65 of the warm-up step, and a conv1-mode tower convolution
 # of the 16384-board forward.
-BACKWARD_TRAFFIC_BYTES = 23662336 + 3840
+BACKWARD_TRAFFIC_BYTES = 23654656 + 3840
 # smsp__inst_executed.sum over the 128 backward launches of one step of this
 # workload (ncu launch list, profiles/backward_cta_search4096x128.md)
-BACKWARD_WARP_INST_PER_STEP = 25896082646
+BACKWARD_WARP_INST_PER_STEP = 25875513797
 CONV_TRAFFIC_BYTES = 420069888 + 370689536
 
 
