@@ -238,7 +238,7 @@ def read_tensor_peak() -> tuple[float, str]:
         return 1590.0, "fallback"
 
 
-def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
+def tower_bench(steps: int, warmup: int, precision: str | None = None) -> dict:
     """Residual tower alone: 16384 boards of {0,1} planes (density 0.4),
     He-normal weights on every layer (seed 0), 16-bit operands with fp32
     accumulation.  Inputs (12.7 MB of planes) are resident; the activations
@@ -248,7 +248,8 @@ def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
     from oracle.network_ref import observations  # input generator only
     from scacchi_b200.network import AZDirichletNet, init_params
 
-    net = AZDirichletNet(init_params(0), fp16=fp16)
+    net = AZDirichletNet(init_params(0), precision=precision)
+    fp16 = net.fp16
     obs = torch.from_numpy(observations(TOWER_BOARDS, seed=0)).cuda()
     for _ in range(warmup):
         net(obs)
@@ -285,7 +286,7 @@ def tower_bench(steps: int, warmup: int, fp16: bool = False) -> dict:
     peak, kind = read_tensor_peak()
     conv_tflops = CONV_FLOP_PER_BOARD * TOWER_BOARDS / (conv_ms / 1e3) / 1e12
     return {
-        "boards": TOWER_BOARDS, "dtype": "fp16" if fp16 else "bf16", "ms_per_forward": round(ms, 4),
+        "boards": TOWER_BOARDS, "dtype": net.precision, "ms_per_forward": round(ms, 4),
         "evals_per_s": round(TOWER_BOARDS / (ms / 1e3), 1),
         "tflops": round(TOWER_FLOP_PER_BOARD * TOWER_BOARDS / (ms / 1e3) / 1e12, 2),
         "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel", "achieved": round(conv_tflops, 2), "peak": peak,
@@ -318,7 +319,7 @@ def population_config(sims: int):
                                                         policy_sample_chunk_size=32)))
 
 
-def full_step_bench(steps: int, warmup: int, fp16: bool = False, population: bool = False, world: int = 1,
+def full_step_bench(steps: int, warmup: int, precision: str | None = None, population: bool = False, world: int = 1,
                     rank: int = 0) -> dict:
     """The full self-play search step: Hex 9x9, 8192 lanes per GPU, 256
     simulations (tree capacity 257), the 6x128 AZDirichletNet with the
@@ -342,7 +343,7 @@ def full_step_bench(steps: int, warmup: int, fp16: bool = False, population: boo
 
     sharding = LaneSharding(world, rank)
     game = HexGame(9)
-    net = AZDirichletNet(init_params(0, he_all_layers=False), fp16=fp16)
+    net = AZDirichletNet(init_params(0, he_all_layers=False), precision=precision)
     evaluator = make_evaluator(net)
     tower_ms = []
     stream = torch.cuda.current_stream()
@@ -394,7 +395,7 @@ def full_step_bench(steps: int, warmup: int, fp16: bool = False, population: boo
         "workload": f"full search step: Hex 9x9, {FULL_LANES} lanes/GPU x {FULL_SIMS} simulations, AZDirichletNet "
                     f"6x128 (reference random init) on the tcgen05 tower, {estimator}, roots 0-20 random moves",
         "lanes": lanes, "lanes_per_gpu": FULL_LANES, "num_simulations": FULL_SIMS,
-        "dtype": "fp16" if fp16 else "bf16", "n_gpus": world,
+        "dtype": net.precision, "n_gpus": world,
         "ms_per_step": round(ms, 2), "sims_per_s": round(lanes * FULL_SIMS / (ms / 1e3), 1),
         "leaf_evals_per_s": round(lanes * (FULL_SIMS + 1) / (ms / 1e3), 1),
         "tower_share": round(t_tower / ms, 4),
@@ -476,7 +477,8 @@ def main() -> None:
                          "full: the full Hex search step with the tower evaluating leaves (1 GPU); "
                          "population: the full step with the 64-sample Thompson-population estimator, "
                          "lane-sharded over the ranks")
-    ap.add_argument("--fp16", action="store_true", help="tower: fp16 operands instead of bf16")
+    ap.add_argument("--precision", default=None,
+                    help="tower precision (scacchi_b200.network.PRECISIONS; default: the library default)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling mode: warmup steps + one device-resident step, no JSON line "
                          "(for ncu captures of the bench workload)")
@@ -501,14 +503,14 @@ def main() -> None:
             from oracle.network_ref import observations
             from scacchi_b200.network import AZDirichletNet, init_params
 
-            net = AZDirichletNet(init_params(0), fp16=args.fp16)
+            net = AZDirichletNet(init_params(0), precision=args.precision)
             obs = torch.from_numpy(observations(TOWER_BOARDS, seed=0)).cuda()
             for _ in range(args.warmup + 1):
                 net(obs)
             torch.cuda.synchronize()
             return
         if rank == 0:
-            t = tower_bench(args.steps, args.warmup, args.fp16)
+            t = tower_bench(args.steps, args.warmup, args.precision)
             print(json.dumps({"metric": "residual tower leaf evals/s (16384 boards)", "value": t["evals_per_s"],
                               "unit": "evals/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
                               "ms_per_step": t["ms_per_forward"], "higher_is_better": True, "scaling": "weak",
@@ -526,7 +528,7 @@ def main() -> None:
         if world > 1:
             dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
         with ClockSampler(local) as clocks:
-            f = full_step_bench(args.steps, args.warmup, args.fp16, population, world, rank)
+            f = full_step_bench(args.steps, args.warmup, args.precision, population, world, rank)
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": f["sims_per_s"], "unit": "sims/s", "n_gpus": world,
                               "steps": args.steps, "warmup": args.warmup, "ms_per_step": f["ms_per_step"],

@@ -338,10 +338,12 @@ uint64_t scacchi_hex_launch_count(void);
  *   stem_w      float32 [9 taps (ky*3+kx)][in_planes][128], stem_b [128]
  *   bn_scale/shift float32 [num_blocks + 1][128]: BN1 of every block, then
  *               the trunk's final BN, as y = x * scale + shift
- *   conv_w      16-bit [2 * num_blocks][9 taps][128 out][128 in] (bf16, or
- *               fp16 when fp16 = 1); the BN after
- *               each block's first conv is folded into that conv's weights
- *               and bias; conv_b float32 [2 * num_blocks][128]
+ *   conv_w      16-bit [2 * num_blocks][parts][9 taps][128 out][128 in]
+ *               (bf16, or fp16 when fp16 = 1), parts = 2 when terms = 3
+ *               (the weight rounded to 16 bits, then the remainder rounded
+ *               to 16 bits), else 1; the BN after each block's first conv
+ *               is folded into that conv's weights and bias; conv_b float32
+ *               [2 * num_blocks][128]
  *   head_w      float32 [6][128], head_b [6]: 1x1 convs of the policy (2),
  *               value (1), Q-mean (2) and Q-concentration (1) heads with
  *               their BNs folded
@@ -350,6 +352,11 @@ uint64_t scacchi_hex_launch_count(void);
 typedef struct {
   int32_t num_blocks, channels, height, width, in_planes, num_actions;
   int32_t fp16;  /* 16-bit operand and activation type: 0 bf16, 1 fp16 */
+  /* tensor-core products per K step: 1 = 16-bit activations and weights,
+   * 16-bit residual stream (the reference's bf16 model); 2 = activations
+   * split into hi + lo 16-bit matrices (A_hi W + A_lo W); 3 = weights split
+   * too (+ A_hi W_lo).  With 2 or 3 the residual stream stays fp32. */
+  int32_t terms;
   const float *stem_w, *stem_b;
   const float *bn_scale, *bn_shift;
   const uint16_t *conv_w;
@@ -367,14 +374,16 @@ typedef struct {
 
 /* Rows of one padded activation matrix for `boards` boards (100 rows per
  * board, rounded up to the 128-row tile) and the workspace the forward
- * pass needs (three bf16 [rows, 128] activations + head features). */
+ * pass needs with any `terms` (split operands: an fp32 [rows, 128] residual
+ * stream and four 16-bit [rows, 128] matrices; head features). */
 uint64_t scacchi_tower_rows(int32_t boards);
 size_t scacchi_tower_workspace_bytes(int32_t boards);
 
-/* AZDirichletNet.__call__(obs, train=False): obs float32 [B, 9, 9, planes]
- * -> logits [B, A], log alpha_v [B, 2], log alpha_q [B, A, 2] (log
- * concentration + log softmax of the mean logits) and the alphas
- * themselves.  bf16 tensor-core convolutions, fp32 accumulation. */
+/* AZDirichletNet.__call__(obs, train=False) (network.py:460-524): obs
+ * float32 [B, 9, 9, planes] -> logits [B, A], log alpha_v [B, 2], log
+ * alpha_q [B, A, 2] (log concentration + log softmax of the mean logits)
+ * and the alphas themselves.  16-bit tensor-core convolutions (1, 2 or 3
+ * products per K step, weights->terms), fp32 accumulation. */
 int scacchi_tower_forward(const scacchi_tower_weights *weights, const float *obs, int32_t boards, void *workspace,
                           float *logits, float *log_alpha_v, float *log_alpha_q, float *alpha_v, float *alpha_q,
                           void *stream);
@@ -389,6 +398,19 @@ int scacchi_conv3x3(const void *input, const void *weights, const float *bias, i
                     int32_t fp16, const float *bn_scale, const float *bn_shift, const void *residual,
                     const float *head_w, const float *head_b, void *out0, void *out1, float *head_out,
                     void *stream);
+
+/* The same convolution on split operands (terms 2 or 3): the input is the
+ * pair input (hi) + input_lo of 16-bit matrices, weights [terms == 3 ? 2 :
+ * 1][9][128 out][128 in], and the residual stream x32 float32 [rows, 128].
+ * mode 0: (out_hi, out_lo) = split(relu(conv + bias)); mode 1: x32 <- x' =
+ * conv + bias + x32 (in place), (out_hi, out_lo) = split(relu(x' *
+ * bn_scale + bn_shift)); mode 2: as mode 1 without the stores, then the six
+ * 1x1 head channels from the fp32 activation into head_out.  split(v): hi =
+ * v rounded to 16 bits, lo = (v - hi) rounded to 16 bits. */
+int scacchi_conv3x3_split(const void *input, const void *input_lo, const void *weights, const float *bias,
+                          int32_t mode, int32_t boards, int32_t fp16, int32_t terms, const float *bn_scale,
+                          const float *bn_shift, float *x32, const float *head_w, const float *head_b, void *out_hi,
+                          void *out_lo, float *head_out, void *stream);
 
 /* Sticky tower error flags (bit 0: a bounded wait timed out); reading
  * synchronises and clears.  Launch counter of the tower kernels. */

@@ -55,7 +55,7 @@ class TowerWeights(C.Structure):
                 "policy_b", "value_w1", "value_b1", "value_mean_w", "value_mean_b", "value_conc_w", "value_conc_b",
                 "qdir_w1", "qdir_b1", "qdir_w2", "qdir_b2", "qconc_w1", "qconc_b1", "qconc_w2", "qconc_b2")
     _fields_ = [(n, C.c_int32) for n in ("num_blocks", "channels", "height", "width", "in_planes", "num_actions",
-                                         "fp16")] + [
+                                         "fp16", "terms")] + [
         (n, C.c_void_p) for n in POINTERS]
 
 
@@ -99,6 +99,7 @@ SIGNATURES = {
     "scacchi_tower_workspace_bytes": [I32],
     "scacchi_tower_forward": [C.POINTER(TowerWeights), P, I32, P, P, P, P, P, P, P],
     "scacchi_conv3x3": [P, P, P, I32, I32, I32, P, P, P, P, P, P, P, P, P],
+    "scacchi_conv3x3_split": [P, P, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P],
     "scacchi_tower_error": [P],
     "scacchi_tower_launch_count": [],
     "scacchi_device_error": [P],

@@ -330,10 +330,12 @@ enum EpiMode : int { kEpiConv1 = 0, kEpiConv2 = 1, kEpiHeads = 2 };
 struct EpiParams {
   int mode;
   int rows_valid;            // E * 100; rows at or above are padding
+  int terms;                 // products per K step: 1; split operands 2 (A hi, lo) or 3 (+ W lo x A hi)
   const float *bias;         // [128] (BatchNorm after conv1 folded in)
   const float *bn_scale;     // conv2: next block's BN1 (or the final BN), per channel
   const float *bn_shift;
   const void *residual;      // conv2 / heads: x of the block input, [rows, 128] 16-bit
+  float *x32;                // split operands: the fp32 residual stream [rows, 128], updated in place
   const float *head_w;       // heads: [6][128] 1x1 conv weights (head BN folded)
   const float *head_b;       // [6]
   float *head_out;           // heads: [rows, 8] f32
@@ -370,7 +372,7 @@ static_assert(SmemLayout::kBytes <= 227 * 1024, "shared memory budget");
 // one row of the tile (its warp's TMEM lane quadrant) and 64 of the 128
 // columns (`half`); the two warps of a quadrant split the columns.  `head`
 // returns the row's partial head sums over its columns.
-template <typename T>
+template <typename T, bool Split>
 __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const float *prm, uint32_t acc_addr, int tile,
                                               int quad, int half, int lane, uint8_t *out0, uint8_t *out1,
                                               float (&head)[kHeadCh]) {
@@ -383,21 +385,38 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const float *
   for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
     // the residual's global loads go out before the accumulator read waits
     uint4 ru[4];
+    float4 rf[8];  // split operands: the fp32 residual stream
     if (ep.mode != kEpiConv1) {
-      const uint4 *src =
-          reinterpret_cast<const uint4 *>(static_cast<const T *>(ep.residual) + (size_t)r * kC + ch * 32);
+      if (Split) {
+        const float4 *src = reinterpret_cast<const float4 *>(ep.x32 + (size_t)r * kC + ch * 32);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) ru[q] = real ? src[q] : make_uint4(0, 0, 0, 0);
+        for (int q = 0; q < 8; ++q) rf[q] = real ? src[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      } else {
+        const uint4 *src =
+            reinterpret_cast<const uint4 *>(static_cast<const T *>(ep.residual) + (size_t)r * kC + ch * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ru[q] = real ? src[q] : make_uint4(0, 0, 0, 0);
+      }
     }
     float v[32];
     tmem_ld32(acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ch * 32), v);
     float res[32];
     if (ep.mode != kEpiConv1) {
+      if (Split) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const T *hb = reinterpret_cast<const T *>(&ru[q]);
+        for (int q = 0; q < 8; ++q) {
+          res[4 * q] = rf[q].x;
+          res[4 * q + 1] = rf[q].y;
+          res[4 * q + 2] = rf[q].z;
+          res[4 * q + 3] = rf[q].w;
+        }
+      } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) res[q * 8 + e] = F16Traits<T>::to_f(hb[e]);
+        for (int q = 0; q < 4; ++q) {
+          const T *hb = reinterpret_cast<const T *>(&ru[q]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) res[q * 8 + e] = F16Traits<T>::to_f(hb[e]);
+        }
       }
     }
     uint32_t pk0[16], pk1[16];
@@ -413,11 +432,14 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const float *
           o0[j] = y;
           o1[j] = 0.0f;
         } else {
-          // residual stream stored in the 16-bit type like the reference's bf16 model
-          const float xn = F16Traits<T>::to_f(F16Traits<T>::from_f(y + res[i + j]));
+          // residual stream stored in the 16-bit type like the reference's
+          // bf16 model, or fp32 with split operands (whose heads then read
+          // the fp32 activation)
+          const float xs = y + res[i + j];
+          const float xn = Split ? xs : F16Traits<T>::to_f(F16Traits<T>::from_f(xs));
           const float a = fmaxf(fmaf(xn, prm[kC + n], prm[2 * kC + n]), 0.0f);
           o0[j] = real ? xn : 0.0f;
-          o1[j] = real ? F16Traits<T>::to_f(F16Traits<T>::from_f(a)) : 0.0f;
+          o1[j] = real ? (Split ? a : F16Traits<T>::to_f(F16Traits<T>::from_f(a))) : 0.0f;
           if (ep.mode == kEpiHeads) {
 #pragma unroll
             for (int h = 0; h < kHeadCh; ++h) head[h] = fmaf(o1[j], prm[3 * kC + h * kC + n], head[h]);
@@ -530,6 +552,81 @@ __device__ __forceinline__ void epilogue_tile_tr(const EpiParams &ep, const floa
   }
 }
 
+// Split operands (terms >= 2): as epilogue_tile_tr, but every 16-bit output
+// is written as a pair, hi = the value rounded to T into out0 and lo = the
+// remainder (exact in fp32) rounded to T into out1, so hi + lo carries about
+// twice T's significand into the next convolution; and the residual stream
+// x stays fp32 in ep.x32 (row-major [rows, 128], read and rewritten in place
+// element by element: for one (block, m) the warp covers 8 rows x 8
+// channels, whole 32-byte sectors).  conv1 writes h's pair; conv2 writes
+// x' = conv + bias + x to x32 and the pair of relu(bn(x')).
+template <typename T>
+__device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, const float (&cst)[3][4],
+                                                       uint32_t acc_addr, int tile, int quad, int wh, int lane,
+                                                       uint8_t *out0, uint8_t *out1) {
+  const bool conv2 = ep.mode == kEpiConv2;
+  uint8_t *h0 = out0 + (quad >> 1) * kTileBytes;
+  uint8_t *h1 = out1 + (quad >> 1) * kTileBytes;
+  const int row_base = wh * 64, chunk0 = (quad & 1) * 4;
+  const int mrow = lane & 7, mat = lane >> 3;
+  const uint32_t lane_addr = acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)row_base;
+  const int ch0 = quad * 32 + lane / 4;  // + 8 m: this thread's channels
+#pragma unroll 1
+  for (int jj = 0; jj < 4; ++jj) {
+    uint32_t d[2][2][4];  // [block of the two][lane group][fragment register]
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2)
+#pragma unroll
+      for (int g = 0; g < 2; ++g) tmem_ld16x256(lane_addr + ((uint32_t)(16 * g) << 16) + 8 * (2 * jj + j2), d[j2][g]);
+    // the residual's loads go out while the accumulator read is in flight
+    float rx[2][4][2];
+    if (conv2) {
+#pragma unroll
+      for (int j2 = 0; j2 < 2; ++j2) {
+        const size_t r0 = (size_t)tile * kBM + row_base + 8 * (2 * jj + j2) + 2 * (lane & 3);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          rx[j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
+          rx[j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+        }
+      }
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2) {
+      const int rb = row_base + 8 * (2 * jj + j2);  // first row of the 8-row block in the tile
+      const int r0 = tile * kBM + rb + 2 * (lane & 3);
+      const bool real0 = row_real(ep, r0), real1 = row_real(ep, r0 + 1);
+      const int srow = rb + mrow, schunk = chunk0 + mat;
+      uint32_t p0[4], p1[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int g = m >> 1, hi = m & 1;
+        const float y0 = __uint_as_float(d[j2][g][2 * hi]) + cst[0][m];
+        const float y1 = __uint_as_float(d[j2][g][2 * hi + 1]) + cst[0][m];
+        float v0, v1;
+        if (!conv2) {
+          v0 = real0 ? fmaxf(y0, 0.0f) : 0.0f;
+          v1 = real1 ? fmaxf(y1, 0.0f) : 0.0f;
+        } else {
+          const float x0 = real0 ? y0 + rx[j2][m][0] : 0.0f;
+          const float x1 = real1 ? y1 + rx[j2][m][1] : 0.0f;
+          ep.x32[(size_t)r0 * kC + ch0 + 8 * m] = x0;
+          ep.x32[(size_t)(r0 + 1) * kC + ch0 + 8 * m] = x1;
+          v0 = real0 ? fmaxf(fmaf(x0, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
+          v1 = real1 ? fmaxf(fmaf(x1, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
+        }
+        const float a0 = F16Traits<T>::to_f(F16Traits<T>::from_f(v0));
+        const float a1 = F16Traits<T>::to_f(F16Traits<T>::from_f(v1));
+        p0[m] = F16Traits<T>::pack(a0, a1);
+        p1[m] = F16Traits<T>::pack(v0 - a0, v1 - a1);
+      }
+      stmatrix_x4_trans(smem_u32(h0 + swz(srow, schunk)), p0);
+      stmatrix_x4_trans(smem_u32(h1 + swz(srow, schunk)), p1);
+    }
+  }
+}
+
 // heads: the row's two column halves' partial sums, bias, ReLU
 __device__ __forceinline__ void store_heads(const EpiParams &ep, const float *prm, int tile, int row_in_tile,
                                             const float (&lo)[kHeadCh], const float *hi) {
@@ -545,8 +642,17 @@ __device__ __forceinline__ void store_heads(const EpiParams &ep, const float *pr
   dst[1] = make_float4(hb[4], hb[5], 0.0f, 0.0f);
 }
 
-template <typename T>
+// Split operands (Split, ep.terms 2 or 3): the activation comes as two
+// 16-bit matrices, hi and lo, and a pair's K loop runs over four windows
+// (hi and lo of each 64-channel half) through the same two window slots.
+// Per (window, tap) the weight tiles are W_hi, plus W_lo after W_hi for a
+// hi window when terms = 3, so the accumulator receives W_hi A_hi +
+// W_hi A_lo (+ W_lo A_hi): the product of the split operands up to the
+// lo x lo term.  The weight map then holds [terms == 3 ? 2 : 1][9 taps]
+// [128 out][128 in].
+template <typename T, bool Split>
 __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_constant__ CUtensorMap tm_win,
+                                                              const __grid_constant__ CUtensorMap tm_win_lo,
                                                               const __grid_constant__ CUtensorMap tm_w,
                                                               const __grid_constant__ CUtensorMap tm_out0,
                                                               const __grid_constant__ CUtensorMap tm_out1,
@@ -561,7 +667,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   uint64_t *b_full = win_empty + 2;
   uint64_t *b_empty = b_full + kMaxBStages;
   uint64_t *acc_full = b_empty + kMaxBStages;
-  const int nbs = ep.mode == kEpiConv1 ? 6 : (ep.mode == kEpiHeads ? kMaxBStages : kBStages);
+  // weight stages: the staging tiles an epilogue mode leaves unused extend the ring
+  const int nbs = ep.mode == kEpiHeads ? kMaxBStages : (ep.mode == kEpiConv1 && !Split ? 6 : kBStages);
+  // windows per pair (hi and lo of each half with split operands) and the
+  // weight tiles per (window, tap)
+  const int nwin = Split ? 4 : 2;
+  const int wlo_terms = Split && ep.terms == 3 ? 2 : 1;  // weight tiles per tap of a hi window
   // the residual layers run transposed (TMEM lane = output channel, column =
   // row, half the MMA instructions); the heads keep one row per TMEM lane
   const bool tr = ep.mode != kEpiHeads;
@@ -611,20 +722,24 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       uint32_t bphase = 0, b_issued = 0, b_parity = 0;  // per stage: issued?, parity of the last load
       bool stop = false;
       for (int pair = blockIdx.x; pair < num_pairs && !stop && !*abort_flag; pair += gridDim.x) {
-        for (int h = 0; h < 2 && !stop; ++h) {
-          for (int tap = 0; tap < 9; ++tap) {
-            if (!mbar_wait(&b_empty[bstage], bphase ^ 1u, abort_flag)) {
-              stop = true;
-              break;
-            }
-            uint8_t *sb = smem + SmemLayout::kBOff + bstage * kBTileBytes;
-            mbar_expect_tx(&b_full[bstage], kBTileBytes);
-            tma_load_2d(sb, &tm_w, &b_full[bstage], h * kBK, tap * kC);
-            b_issued |= 1u << bstage;
-            b_parity = (b_parity & ~(1u << bstage)) | (bphase << bstage);
-            if (++bstage == nbs) {
-              bstage = 0;
-              bphase ^= 1u;
+        for (int wi = 0; wi < nwin && !stop; ++wi) {
+          const int h = Split ? wi >> 1 : wi;
+          const int nt = Split && (wi & 1) ? 1 : wlo_terms;
+          for (int tap = 0; tap < 9 && !stop; ++tap) {
+            for (int term = 0; term < nt; ++term) {
+              if (!mbar_wait(&b_empty[bstage], bphase ^ 1u, abort_flag)) {
+                stop = true;
+                break;
+              }
+              uint8_t *sb = smem + SmemLayout::kBOff + bstage * kBTileBytes;
+              mbar_expect_tx(&b_full[bstage], kBTileBytes);
+              tma_load_2d(sb, &tm_w, &b_full[bstage], h * kBK, (term * 9 + tap) * kC);
+              b_issued |= 1u << bstage;
+              b_parity = (b_parity & ~(1u << bstage)) | (bphase << bstage);
+              if (++bstage == nbs) {
+                bstage = 0;
+                bphase ^= 1u;
+              }
             }
           }
         }
@@ -642,18 +757,21 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       bool stop = false;
       for (int pair = blockIdx.x; pair < num_pairs && !stop && !*abort_flag; pair += gridDim.x) {
         const int row0 = pair * 2 * kBM;
-        for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&win_empty[h], wphase[h] ^ 1u, abort_flag)) {
+        for (int wi = 0; wi < nwin; ++wi) {
+          const int s = wi & 1;                      // window slot
+          const int h = Split ? wi >> 1 : wi;        // channel half
+          const CUtensorMap *src = Split && (wi & 1) ? &tm_win_lo : &tm_win;
+          if (!mbar_wait(&win_empty[s], wphase[s] ^ 1u, abort_flag)) {
             stop = true;
             break;
           }
-          uint8_t *win = smem + SmemLayout::kWinOff + h * kWinHalfBytes;
-          mbar_expect_tx(&win_full[h], kWinHalfBytes);
-          tma_load_2d(win, &tm_win, &win_full[h], h * kBK, row0 - kWinLead);
-          tma_load_2d(win + kWinBoxRows * 128, &tm_win, &win_full[h], h * kBK, row0 - kWinLead + kWinBoxRows);
-          w_issued |= 1u << h;
-          w_parity = (w_parity & ~(1u << h)) | (wphase[h] << h);
-          wphase[h] ^= 1u;
+          uint8_t *win = smem + SmemLayout::kWinOff + s * kWinHalfBytes;
+          mbar_expect_tx(&win_full[s], kWinHalfBytes);
+          tma_load_2d(win, src, &win_full[s], h * kBK, row0 - kWinLead);
+          tma_load_2d(win + kWinBoxRows * 128, src, &win_full[s], h * kBK, row0 - kWinLead + kWinBoxRows);
+          w_issued |= 1u << s;
+          w_parity = (w_parity & ~(1u << s)) | (wphase[s] << s);
+          wphase[s] ^= 1u;
         }
       }
       for (int h = 0; h < 2; ++h)
@@ -669,48 +787,53 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         tc_fence_after();
         const uint32_t d0 = tmem_base + (uint32_t)(2 * slot * kC);
         bool ok = true;
-        for (int h = 0; h < 2 && ok; ++h) {
-          if (!mbar_wait(&win_full[h], wphase[h], abort_flag)) {
+        for (int wi = 0; wi < nwin && ok; ++wi) {
+          const int s = wi & 1;
+          const int nt = Split && (wi & 1) ? 1 : wlo_terms;
+          if (!mbar_wait(&win_full[s], wphase[s], abort_flag)) {
             ok = false;
             break;
           }
-          wphase[h] ^= 1u;
+          wphase[s] ^= 1u;
           tc_fence_after();
-          const uint32_t win = smem_u32(smem + SmemLayout::kWinOff + h * kWinHalfBytes);
-          for (int tap = 0; tap < 9; ++tap) {
-            if (!mbar_wait(&b_full[bstage], bphase, abort_flag)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t sb = smem_u32(smem + SmemLayout::kBOff + bstage * kBTileBytes);
+          const uint32_t win = smem_u32(smem + SmemLayout::kWinOff + s * kWinHalfBytes);
+          for (int tap = 0; tap < 9 && ok; ++tap) {
             const int off = (tap / 3 - 1) * 10 + (tap % 3 - 1);
-            if (tr) {
-              // D[channel][row] of both sub-tiles: one N = 256 product per K step
-              const uint32_t wrow = win + (uint32_t)(kWinLead + off) * 128u;
+            for (int term = 0; term < nt; ++term) {
+              if (!mbar_wait(&b_full[bstage], bphase, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t sb = smem_u32(smem + SmemLayout::kBOff + bstage * kBTileBytes);
+              const uint32_t acc = (wi | tap | term) != 0;
+              if (tr) {
+                // D[channel][row] of both sub-tiles: one N = 256 product per K step
+                const uint32_t wrow = win + (uint32_t)(kWinLead + off) * 128u;
 #pragma unroll
-              for (int k = 0; k < kBK / 16; ++k)
-                umma_f16(d0, smem_desc_sw128(sb + k * 32), smem_desc_sw128(wrow + k * 32), idesc_tr<T>(),
-                         (h | tap | k) != 0);
-            } else {
+                for (int k = 0; k < kBK / 16; ++k)
+                  umma_f16(d0, smem_desc_sw128(sb + k * 32), smem_desc_sw128(wrow + k * 32), idesc_tr<T>(),
+                           acc | (k != 0));
+              } else {
 #pragma unroll
-              for (int sub = 0; sub < 2; ++sub) {
-                const int w = kWinLead + sub * kBM + off;  // window row of the sub-tile's row 0
+                for (int sub = 0; sub < 2; ++sub) {
+                  const int w = kWinLead + sub * kBM + off;  // window row of the sub-tile's row 0
 #pragma unroll
-                for (int k = 0; k < kBK / 16; ++k) {
-                  const uint64_t adesc = smem_desc_sw128(win + (uint32_t)w * 128u + k * 32);
-                  const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
-                  umma_f16(d0 + (uint32_t)(sub * kC), adesc, bdesc, idesc_for<T>(), (h | tap | k) != 0);
+                  for (int k = 0; k < kBK / 16; ++k) {
+                    const uint64_t adesc = smem_desc_sw128(win + (uint32_t)w * 128u + k * 32);
+                    const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
+                    umma_f16(d0 + (uint32_t)(sub * kC), adesc, bdesc, idesc_for<T>(), acc | (k != 0));
+                  }
                 }
               }
-            }
-            umma_commit(&b_empty[bstage]);
-            if (++bstage == nbs) {
-              bstage = 0;
-              bphase ^= 1u;
+              umma_commit(&b_empty[bstage]);
+              if (++bstage == nbs) {
+                bstage = 0;
+                bphase ^= 1u;
+              }
             }
           }
-          if (ok) umma_commit(&win_empty[h]);
+          if (ok) umma_commit(&win_empty[s]);
         }
         if (!ok) break;
         umma_commit(&acc_full[slot]);
@@ -745,8 +868,13 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     auto prefetch_residual = [&](int p) {
       for (int sub = 0; sub < 2; ++sub) {
         const int tile = p * 2 + sub;
-        if (p < num_pairs && tile < num_tiles)
-          prefetch_l2(static_cast<const T *>(ep.residual) + (size_t)tile * kBM * kC, kBM * kC * (uint32_t)sizeof(T));
+        if (p < num_pairs && tile < num_tiles) {
+          if (Split)
+            prefetch_l2(ep.x32 + (size_t)tile * kBM * kC, kBM * kC * (uint32_t)sizeof(float));
+          else
+            prefetch_l2(static_cast<const T *>(ep.residual) + (size_t)tile * kBM * kC,
+                        kBM * kC * (uint32_t)sizeof(T));
+        }
       }
     };
     if (has_res && et == 0) prefetch_residual(blockIdx.x);
@@ -765,19 +893,22 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int tile = pair * 2 + sub;
         if (tile >= num_tiles) break;  // uniform across the epilogue threads
         uint4 res[8];
-        if (tr && ep.mode == kEpiConv2) load_residual_tr<T>(ep, tile, quad, half, lane, res);
+        if (!Split && tr && ep.mode == kEpiConv2) load_residual_tr<T>(ep, tile, quad, half, lane, res);
         if (ep.mode != kEpiHeads) {
           // the staging buffers are free once the previous store has read them
           if (et == 0) tma_store_wait_read();
           asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
         }
         float head[kHeadCh];
-        if (tr)
+        if (tr && Split)
+          epilogue_tile_tr_split<T>(ep, cst, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane,
+                                    out0, out1);
+        else if (tr)
           epilogue_tile_tr<T>(ep, cst, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0,
                               out1, res);
         else
-          epilogue_tile<T>(ep, prm, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0,
-                           out1, head);
+          epilogue_tile<T, Split>(ep, prm, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane,
+                                  out0, out1, head);
         if (ep.mode == kEpiHeads) {
           const int row_in_tile = quad * 32 + lane;
           if (half == 1) {
@@ -795,7 +926,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
           const int row0 = tile * kBM;
           tma_store_2d(&tm_out0, out0, 0, row0);
           tma_store_2d(&tm_out0, out0 + kTileBytes, kBK, row0);
-          if (ep.mode == kEpiConv2) {
+          if (ep.mode == kEpiConv2 || Split) {
             tma_store_2d(&tm_out1, out1, 0, row0);
             tma_store_2d(&tm_out1, out1 + kTileBytes, kBK, row0);
           }
@@ -843,10 +974,12 @@ size_t stem_smem_bytes(int in_planes) {
   return (size_t)rows * kC * sizeof(float) + kStemBoards * 128;
 }
 
-template <typename T>
+// With split operands (Split) x is written in fp32 to x32 and a as the
+// pair a (hi) / a_lo of 16-bit matrices.
+template <typename T, bool Split>
 __global__ void __launch_bounds__(kStemThreads, 2) stem_kernel(const float *obs, int boards, int in_planes,
                                                             const float *w, const float *b, const float *s1,
-                                                            const float *t1, T *x, T *a) {
+                                                            const float *t1, T *x, T *a, float *x32, T *a_lo) {
   extern __shared__ float sm[];
   const bool table = in_planes <= 4;
   // table: [9 taps][16 subsets][128]; otherwise the weights [9 * in_planes][128]
@@ -952,22 +1085,46 @@ __global__ void __launch_bounds__(kStemThreads, 2) stem_kernel(const float *obs,
         }
       }
     }
-    uint32_t px[4], pa[4];
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      float xv[2], av[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const float xr = F16Traits<T>::to_f(F16Traits<T>::from_f(real ? acc[j + u] : 0.0f));
-        xv[u] = xr;
-        av[u] = real ? fmaxf(fmaf(xr, sc[j + u], sh[j + u]), 0.0f) : 0.0f;
-      }
-      px[j / 2] = F16Traits<T>::pack(xv[0], xv[1]);
-      pa[j / 2] = F16Traits<T>::pack(av[0], av[1]);
-    }
     const size_t r = (size_t)(e0 + eb) * kRowsPerBoard + p;
-    *reinterpret_cast<uint4 *>(x + r * kC + n0) = make_uint4(px[0], px[1], px[2], px[3]);
-    *reinterpret_cast<uint4 *>(a + r * kC + n0) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+    if (Split) {
+      // fp32 x; a as hi + lo
+      float xv[8];
+      uint32_t ph[4], pl[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        float hi[2], lo[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          xv[j + u] = real ? acc[j + u] : 0.0f;
+          const float av = real ? fmaxf(fmaf(xv[j + u], sc[j + u], sh[j + u]), 0.0f) : 0.0f;
+          hi[u] = F16Traits<T>::to_f(F16Traits<T>::from_f(av));
+          lo[u] = av - hi[u];
+        }
+        ph[j / 2] = F16Traits<T>::pack(hi[0], hi[1]);
+        pl[j / 2] = F16Traits<T>::pack(lo[0], lo[1]);
+      }
+      float4 *xd = reinterpret_cast<float4 *>(x32 + r * kC + n0);
+      xd[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
+      xd[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
+      *reinterpret_cast<uint4 *>(a + r * kC + n0) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+      *reinterpret_cast<uint4 *>(a_lo + r * kC + n0) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    } else {
+      uint32_t px[4], pa[4];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        float xv[2], av[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float xr = F16Traits<T>::to_f(F16Traits<T>::from_f(real ? acc[j + u] : 0.0f));
+          xv[u] = xr;
+          av[u] = real ? fmaxf(fmaf(xr, sc[j + u], sh[j + u]), 0.0f) : 0.0f;
+        }
+        px[j / 2] = F16Traits<T>::pack(xv[0], xv[1]);
+        pa[j / 2] = F16Traits<T>::pack(av[0], av[1]);
+      }
+      *reinterpret_cast<uint4 *>(x + r * kC + n0) = make_uint4(px[0], px[1], px[2], px[3]);
+      *reinterpret_cast<uint4 *>(a + r * kC + n0) = make_uint4(pa[0], pa[1], pa[2], pa[3]);
+    }
   }
 }
 
@@ -1179,25 +1336,31 @@ int num_sms() {
   return n;
 }
 
-template <typename T>
-int launch_conv(const void *in, const void *w, void *out0, void *out1, const EpiParams &ep, uint64_t rows_alloc,
-                cudaStream_t stream) {
-  CUtensorMap m_in, m_w, m_o0, m_o1;
-  if (!make_map(&m_in, in, rows_alloc, kWinBoxRows) || !make_map(&m_w, w, 9 * kC)) return SCACCHI_ECUDA;
+// in_lo: the lo matrix of split operands (Split), else unused
+template <typename T, bool Split>
+int launch_conv(const void *in, const void *in_lo, const void *w, void *out0, void *out1, const EpiParams &ep,
+                uint64_t rows_alloc, cudaStream_t stream) {
+  CUtensorMap m_in, m_in_lo, m_w, m_o0, m_o1;
+  const uint64_t w_rows = (uint64_t)9 * kC * (Split && ep.terms == 3 ? 2 : 1);
+  if (!make_map(&m_in, in, rows_alloc, kWinBoxRows) || !make_map(&m_w, w, w_rows)) return SCACCHI_ECUDA;
+  if (!make_map(&m_in_lo, Split ? in_lo : in, rows_alloc, kWinBoxRows)) return SCACCHI_ECUDA;
   if (!make_map(&m_o0, out0 ? out0 : in, rows_alloc)) return SCACCHI_ECUDA;
   if (!make_map(&m_o1, out1 ? out1 : (out0 ? out0 : in), rows_alloc)) return SCACCHI_ECUDA;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(conv_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::kBytes);
+    cudaFuncSetAttribute(conv_tc_kernel<T, Split>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::kBytes);
     attr = true;
   }
   const int tiles = (int)(rows_alloc / kBM);
   const int pairs = (tiles + 1) / 2;
   const int grid = pairs < num_sms() ? pairs : num_sms();
-  conv_tc_kernel<T><<<grid, kThreads, SmemLayout::kBytes, stream>>>(m_in, m_w, m_o0, m_o1, ep, tiles);
+  conv_tc_kernel<T, Split><<<grid, kThreads, SmemLayout::kBytes, stream>>>(m_in, m_in_lo, m_w, m_o0, m_o1, ep,
+                                                                            tiles);
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaPeekAtLastError() == cudaSuccess ? SCACCHI_OK : SCACCHI_ECUDA;
 }
+
+bool misaligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0; }
 
 }  // namespace
 
@@ -1209,8 +1372,9 @@ uint64_t scacchi_tower_rows(int32_t boards) {
 }
 
 size_t scacchi_tower_workspace_bytes(int32_t boards) {
+  // split operands: fp32 x + hi/lo of a and h; plain: three 16-bit matrices
   const uint64_t rows = scacchi_tower_rows(boards);
-  return (size_t)rows * kC * 2 * 3 + (size_t)rows * 8 * 4;
+  return (size_t)rows * kC * (4 + 2 * 4) + (size_t)rows * 8 * 4;
 }
 
 int scacchi_conv3x3(const void *input, const void *weights, const float *bias, int32_t mode, int32_t boards,
@@ -1236,10 +1400,43 @@ int scacchi_conv3x3(const void *input, const void *weights, const float *bias, i
   ep.head_w = head_w;
   ep.head_b = head_b;
   ep.head_out = head_out;
+  ep.terms = 1;
+  ep.x32 = nullptr;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint64_t rows = scacchi_tower_rows(boards);
-  return fp16 ? launch_conv<__half>(input, weights, out0, out1, ep, rows, st)
-              : launch_conv<__nv_bfloat16>(input, weights, out0, out1, ep, rows, st);
+  return fp16 ? launch_conv<__half, false>(input, nullptr, weights, out0, out1, ep, rows, st)
+              : launch_conv<__nv_bfloat16, false>(input, nullptr, weights, out0, out1, ep, rows, st);
+}
+
+int scacchi_conv3x3_split(const void *input, const void *input_lo, const void *weights, const float *bias,
+                          int32_t mode, int32_t boards, int32_t fp16, int32_t terms, const float *bn_scale,
+                          const float *bn_shift, float *x32, const float *head_w, const float *head_b, void *out_hi,
+                          void *out_lo, float *head_out, void *stream) {
+  if (!input || !input_lo || !weights || !bias || boards < 1 || mode < 0 || mode > 2 || (fp16 != 0 && fp16 != 1) ||
+      terms < 2 || terms > 3)
+    return SCACCHI_EINVAL;
+  if (mode != kEpiConv1 && (!bn_scale || !bn_shift || !x32)) return SCACCHI_EINVAL;
+  if (mode == kEpiHeads && (!head_w || !head_b || !head_out)) return SCACCHI_EINVAL;
+  if (mode != kEpiHeads && (!out_hi || !out_lo)) return SCACCHI_EINVAL;
+  if (misaligned16(input) || misaligned16(input_lo) || misaligned16(weights) || misaligned16(out_hi) ||
+      misaligned16(out_lo) || misaligned16(x32))
+    return SCACCHI_EINVAL;
+  EpiParams ep;
+  ep.mode = mode;
+  ep.rows_valid = boards * kRowsPerBoard;
+  ep.terms = terms;
+  ep.bias = bias;
+  ep.bn_scale = bn_scale;
+  ep.bn_shift = bn_shift;
+  ep.residual = nullptr;
+  ep.x32 = x32;
+  ep.head_w = head_w;
+  ep.head_b = head_b;
+  ep.head_out = head_out;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint64_t rows = scacchi_tower_rows(boards);
+  return fp16 ? launch_conv<__half, true>(input, input_lo, weights, out_hi, out_lo, ep, rows, st)
+              : launch_conv<__nv_bfloat16, true>(input, input_lo, weights, out_hi, out_lo, ep, rows, st);
 }
 
 int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int32_t boards, void *workspace,
@@ -1250,48 +1447,76 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
   if (w->channels != kC || w->height != 9 || w->width != 9 || w->num_blocks < 1 || w->in_planes < 1 ||
       w->in_planes > 16 || w->num_actions < 1 || w->num_actions > 256)
     return SCACCHI_EINVAL;
-  if (w->fp16 != 0 && w->fp16 != 1) return SCACCHI_EINVAL;
+  if ((w->fp16 != 0 && w->fp16 != 1) || w->terms < 1 || w->terms > 3) return SCACCHI_EINVAL;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint64_t rows = scacchi_tower_rows(boards);
+  const bool split = w->terms > 1;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  uint16_t *x = reinterpret_cast<uint16_t *>(ws);
-  uint16_t *a = x + rows * kC;
-  uint16_t *h = a + rows * kC;
-  float *feat = reinterpret_cast<float *>(h + rows * kC);
+  // plain: x, a, h 16-bit; split: x fp32, then the hi/lo pairs of a and h
+  float *x32 = split ? reinterpret_cast<float *>(ws) : nullptr;
+  uint16_t *x = split ? nullptr : reinterpret_cast<uint16_t *>(ws);
+  uint16_t *a = split ? reinterpret_cast<uint16_t *>(x32 + rows * kC) : x + rows * kC;
+  uint16_t *a_lo = split ? a + rows * kC : nullptr;
+  uint16_t *h = split ? a_lo + rows * kC : a + rows * kC;
+  uint16_t *h_lo = split ? h + rows * kC : nullptr;
+  float *feat = reinterpret_cast<float *>((split ? h_lo : h) + rows * kC);
   // rows past the last board stay zero (they are padding for the last tile)
   const uint64_t used = (uint64_t)boards * kRowsPerBoard;
   if (rows > used) {
-    cudaMemsetAsync(x + used * kC, 0, (rows - used) * kC * 2, st);
+    if (split) {
+      cudaMemsetAsync(x32 + used * kC, 0, (rows - used) * kC * 4, st);
+      cudaMemsetAsync(a_lo + used * kC, 0, (rows - used) * kC * 2, st);
+    } else {
+      cudaMemsetAsync(x + used * kC, 0, (rows - used) * kC * 2, st);
+    }
     cudaMemsetAsync(a + used * kC, 0, (rows - used) * kC * 2, st);
   }
   const size_t smem = stem_smem_bytes(w->in_planes);
   const int stem_grid = (boards + kStemBoards - 1) / kStemBoards;
   static std::atomic<size_t> stem_attr{0};
   if (smem > 48 * 1024 && stem_attr.load() < smem) {
-    cudaFuncSetAttribute(stem_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(stem_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(stem_kernel<__half, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(stem_kernel<__nv_bfloat16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(stem_kernel<__half, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(stem_kernel<__nv_bfloat16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     stem_attr.store(smem);
   }
-  if (w->fp16)
-    stem_kernel<__half><<<stem_grid, kStemThreads, smem, st>>>(obs, boards, w->in_planes, w->stem_w, w->stem_b,
-                                                               w->bn_scale, w->bn_shift, reinterpret_cast<__half *>(x),
-                                                               reinterpret_cast<__half *>(a));
-  else
-    stem_kernel<__nv_bfloat16><<<stem_grid, kStemThreads, smem, st>>>(
-        obs, boards, w->in_planes, w->stem_w, w->stem_b, w->bn_scale, w->bn_shift,
-        reinterpret_cast<__nv_bfloat16 *>(x), reinterpret_cast<__nv_bfloat16 *>(a));
+#define SCACCHI_STEM(TT, SPLIT)                                                                                     \
+  stem_kernel<TT, SPLIT><<<stem_grid, kStemThreads, smem, st>>>(                                                   \
+      obs, boards, w->in_planes, w->stem_w, w->stem_b, w->bn_scale, w->bn_shift, reinterpret_cast<TT *>(x),        \
+      reinterpret_cast<TT *>(a), x32, reinterpret_cast<TT *>(a_lo))
+  if (w->fp16) {
+    if (split) SCACCHI_STEM(__half, true);
+    else SCACCHI_STEM(__half, false);
+  } else {
+    if (split) SCACCHI_STEM(__nv_bfloat16, true);
+    else SCACCHI_STEM(__nv_bfloat16, false);
+  }
+#undef SCACCHI_STEM
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
-  const size_t conv_elems = (size_t)9 * kC * kC;
+  // per layer: [terms == 3 ? 2 : 1][9 taps][128 out][128 in]
+  const size_t conv_elems = (size_t)9 * kC * kC * (w->terms == 3 ? 2 : 1);
   for (int blk = 0; blk < w->num_blocks; ++blk) {
     const uint16_t *w1 = w->conv_w + (size_t)(2 * blk) * conv_elems;
     const uint16_t *w2 = w->conv_w + (size_t)(2 * blk + 1) * conv_elems;
-    int rc = scacchi_conv3x3(a, w1, w->conv_b + (2 * blk) * kC, kEpiConv1, boards, w->fp16, nullptr, nullptr,
-                             nullptr, nullptr, nullptr, h, nullptr, nullptr, stream);
-    if (rc) return rc;
     const bool last = blk == w->num_blocks - 1;
-    rc = scacchi_conv3x3(h, w2, w->conv_b + (2 * blk + 1) * kC, last ? kEpiHeads : kEpiConv2, boards, w->fp16,
-                         w->bn_scale + (blk + 1) * kC, w->bn_shift + (blk + 1) * kC, x, w->head_w, w->head_b,
-                         last ? nullptr : x, last ? nullptr : a, feat, stream);
+    const int mode2 = last ? kEpiHeads : kEpiConv2;
+    const float *s2 = w->bn_scale + (blk + 1) * kC, *t2 = w->bn_shift + (blk + 1) * kC;
+    int rc;
+    if (split) {
+      rc = scacchi_conv3x3_split(a, a_lo, w1, w->conv_b + (2 * blk) * kC, kEpiConv1, boards, w->fp16, w->terms,
+                                 nullptr, nullptr, nullptr, nullptr, nullptr, h, h_lo, nullptr, stream);
+      if (rc) return rc;
+      rc = scacchi_conv3x3_split(h, h_lo, w2, w->conv_b + (2 * blk + 1) * kC, mode2, boards, w->fp16, w->terms, s2,
+                                 t2, x32, w->head_w, w->head_b, last ? nullptr : a, last ? nullptr : a_lo, feat,
+                                 stream);
+    } else {
+      rc = scacchi_conv3x3(a, w1, w->conv_b + (2 * blk) * kC, kEpiConv1, boards, w->fp16, nullptr, nullptr, nullptr,
+                           nullptr, nullptr, h, nullptr, nullptr, stream);
+      if (rc) return rc;
+      rc = scacchi_conv3x3(h, w2, w->conv_b + (2 * blk + 1) * kC, mode2, boards, w->fp16, s2, t2, x, w->head_w,
+                           w->head_b, last ? nullptr : x, last ? nullptr : a, feat, stream);
+    }
     if (rc) return rc;
   }
   HeadWeights hw;
