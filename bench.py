@@ -479,6 +479,8 @@ def main() -> None:
                          "lane-sharded over the ranks")
     ap.add_argument("--precision", default=None,
                     help="tower precision (scacchi_b200.network.PRECISIONS; default: the library default)")
+    ap.add_argument("--boards", type=int, default=TOWER_BOARDS,
+                    help="tower --profile: boards per forward (smaller cases for ncu captures)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling mode: warmup steps + one device-resident step, no JSON line "
                          "(for ncu captures of the bench workload)")
@@ -504,7 +506,7 @@ def main() -> None:
             from scacchi_b200.network import AZDirichletNet, init_params
 
             net = AZDirichletNet(init_params(0), precision=args.precision)
-            obs = torch.from_numpy(observations(TOWER_BOARDS, seed=0)).cuda()
+            obs = torch.from_numpy(observations(args.boards, seed=0)).cuda()
             for _ in range(args.warmup + 1):
                 net(obs)
             torch.cuda.synchronize()

@@ -437,12 +437,17 @@ class PolicyOutput(NamedTuple):
 
 def dirichlet_thompson_policy(rng_key, *, root: dict, recurrent_fn: Callable, num_simulations: int,
                               invalid_actions=None, rule: Rule = Rule(prefix_cdf=False), max_depth=None,
-                              policy_samples: int = 32) -> PolicyOutput:
+                              policy_samples: int = 32, lane_offset: int = 0,
+                              total_batch: int = 0) -> PolicyOutput:
     """policies.py:17-48 + search.py:189-251 driven from Python.
 
     ``root``: dict with value [B,2], action_values [B,A,2], terminal_outcome,
     to_play, prior_logits and optionally embedding [B,E] (uint8 rows).
     ``recurrent_fn(action, parent_embedding) -> (step dict, child_embedding)``.
+    The B lanes may be lanes [lane_offset, lane_offset + B) of a batch of
+    ``total_batch`` lanes: lane-indexed and batch-wide random streams then
+    use the lanes' places in that batch (bit-identical to the same lanes of
+    a full run).
     """
     if max_depth is None:
         max_depth = num_simulations
@@ -454,6 +459,7 @@ def dirichlet_thompson_policy(rng_key, *, root: dict, recurrent_fn: Callable, nu
     emb = root.get("embedding")
     tree = tree_init(root["value"], root["action_values"], invalid_actions, root["terminal_outcome"],
                      root["to_play"], num_simulations, emb)
+    tree.lane_offset, tree.total_batch = int(lane_offset), int(total_batch)
     unsafe = 0
     key = search_key
     B = tree.dims[0]
@@ -552,6 +558,36 @@ def root_readout(native, summary: dict, legal, *, search_evidence: bool, tempera
 # --------------------------------------------------------------------------
 # action commitment
 # --------------------------------------------------------------------------
+
+TARGET_PAD, TARGET_DIRICHLET, TARGET_CATEGORICAL = 0, 1, 2
+
+
+def pack_targets(summary: dict, policy_target, legal, search_action) -> dict:
+    """play_search.py:490-548 (_run_dirichlet_thompson_search's target
+    packing) with dirichlet_q_search.py:119-182 (build_q_supervision) for
+    the default QSupervisionConfig (positive search evidence or solved;
+    mean over selected state-action pairs).  numpy in, numpy out; keys are
+    the PosteriorTargets field names."""
+    legal = np.asarray(legal, bool)
+    policy_target = np.asarray(policy_target, np.float32)
+    q_count = summary["visit_counts"][..., None]
+    q_cat = summary["q_categorical_outcome"] != -1
+    v_cat = summary["v_categorical_outcome"] != -1
+    q_kind = np.where(legal, np.where(q_cat, TARGET_CATEGORICAL, TARGET_DIRICHLET), TARGET_PAD).astype(np.int8)
+    v_kind = np.where(v_cat, TARGET_CATEGORICAL, TARGET_DIRICHLET).astype(np.int8)
+    positive_evidence = q_count.sum(-1) > 0
+    selected = legal & (positive_evidence | q_cat)
+    return dict(
+        policy=policy_target, alpha_q=summary["alpha"], alpha_v=summary["value_alpha"],
+        mask=policy_target.sum(-1) > 0, q_supervision_selected=selected,
+        q_supervision_pair_weight=selected.astype(np.float32),
+        q_positive_evidence_action=legal & positive_evidence, q_positive_policy_action=legal & (policy_target > 0),
+        search_action=np.asarray(search_action, np.int32), q_target_kind=q_kind,
+        q_target_weight=legal.astype(np.float32), q_target_outcome=summary["q_categorical_outcome"],
+        q_target_distance=summary["q_categorical_distance"], v_target_kind=v_kind,
+        v_target_weight=np.ones_like(summary["v_categorical_distance"], np.float32),
+        v_target_outcome=summary["v_categorical_outcome"], v_target_distance=summary["v_categorical_distance"])
+
 
 def commitment_policy(sampled, search_action, alpha, q_outcome, v_outcome, legal, evidence, *,
                       search_evidence: bool, numerical: bool, rule: Rule = Rule()) -> np.ndarray:

@@ -211,8 +211,9 @@ def dirichlet_root_policy_readout(native_policy: torch.Tensor, summary, legal_ac
 def run_dirichlet_thompson_search(env_state, prediction: EvaluatorOutput, expand_fn, rng_key,
                                   search_cfg: DirichletThompsonSearchConfig,
                                   q_supervision_config: QSupervisionConfig, embedding: Any = None,
-                                  stats: torch.Tensor | None = None) -> PosteriorTargets:
-    """play_search.py:435-548."""
+                                  stats: torch.Tensor | None = None, record: dict | None = None) -> PosteriorTargets:
+    """play_search.py:435-548.  ``record``, when given, receives the search's
+    PolicyOutput (tree included) under "policy_output"."""
     alpha_v = _required_output(prediction.alpha_v, "alpha_v")
     alpha_q = _required_output(prediction.alpha_q, "alpha_q")
     B = env_state.rewards.shape[0]
@@ -232,6 +233,8 @@ def run_dirichlet_thompson_search(env_state, prediction: EvaluatorOutput, expand
                                     posterior_update=_make_posterior_update(update_cfg),
                                     max_depth=search_cfg.max_depth, policy_samples=samples,
                                     policy_sample_chunk_size=chunk, stats=stats)
+    if record is not None:
+        record["policy_output"] = out
     summary = out.search_tree.summary()
     policy_target = dirichlet_root_policy_readout(out.action_weights, summary, legal, search_cfg)
     beta_q, beta_v = summary.alpha, summary.value_alpha
@@ -259,8 +262,11 @@ def run_dirichlet_thompson_search(env_state, prediction: EvaluatorOutput, expand
 
 def make_search(env, evaluator: Callable, search_cfg: SearchConfig | DirichletThompsonSearchConfig,
                 q_supervision_config: QSupervisionConfig | None = None,
-                stats: torch.Tensor | None = None) -> Search:
-    """play_search.py:609-624 for the dirichlet_thompson kind."""
+                stats: torch.Tensor | None = None, keep_output: bool = False) -> Search:
+    """play_search.py:609-624 for the dirichlet_thompson kind.  With
+    ``keep_output`` the returned function keeps its last call's PolicyOutput
+    (action, action_weights, search_tree) in ``search.last_output`` for
+    inspection; the tree then stays allocated until the next call."""
     if q_supervision_config is None:
         q_supervision_config = QSupervisionConfig()
     if isinstance(search_cfg, SearchConfig):
@@ -273,11 +279,16 @@ def make_search(env, evaluator: Callable, search_cfg: SearchConfig | DirichletTh
 
     def search(root_state, rng_key) -> PosteriorTargets:
         prediction = evaluator(root_state.observation)
-        return run_dirichlet_thompson_search(root_state, prediction, expand_fn, rng_key, search_cfg,
-                                             q_supervision_config,
-                                             embedding=embed(root_state) if embed is not None else None,
-                                             stats=stats)
+        record = {} if keep_output else None
+        targets = run_dirichlet_thompson_search(root_state, prediction, expand_fn, rng_key, search_cfg,
+                                                q_supervision_config,
+                                                embedding=embed(root_state) if embed is not None else None,
+                                                stats=stats, record=record)
+        if keep_output:
+            search.last_output = record["policy_output"]
+        return targets
 
+    search.last_output = None
     return search
 
 
