@@ -417,6 +417,15 @@ int scacchi_conv3x3_split(const void *input, const void *input_lo, const void *w
 int scacchi_tower_error(uint32_t *flags);
 uint64_t scacchi_tower_launch_count(void);
 
+/* Optional timing of the tower's convolutions (no reference counterpart:
+ * measurement only).  scacchi_tower_timing(n) makes the next n forwards
+ * record a CUDA event pair around their conv launches on their stream (0
+ * turns it off); scacchi_tower_timing_read waits for those events and
+ * returns the summed conv time (ms) and the number of forwards timed, then
+ * starts counting again. */
+int scacchi_tower_timing(int32_t max_forwards);
+int scacchi_tower_timing_read(float *conv_ms, int32_t *forwards);
+
 /* ---- host-side jax.random key helpers (no device work) ---------------- */
 
 /* search.py:207-209 key chain: for i < num_simulations,

@@ -102,6 +102,8 @@ SIGNATURES = {
     "scacchi_conv3x3_split": [P, P, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P],
     "scacchi_tower_error": [P],
     "scacchi_tower_launch_count": [],
+    "scacchi_tower_timing": [I32],
+    "scacchi_tower_timing_read": [P, P],
     "scacchi_device_error": [P],
     "scacchi_launch_count": [],
 }

@@ -26,7 +26,8 @@
  *   sm_erfinvf Giles, "Approximating the erfinv function" (GPU Computing
  *              Gems Jade, 2011), single-precision coefficients as published.
  *
- * Accuracy (tests/test_smath.py, against float64): log/exp/log1p <= 2 ulp,
+ * Accuracy (tests/test_oracle_pins.py: test_scalar_math_accuracy,
+ * test_erfinv_tail, test_lgamma_and_betaln; against float64): log/exp/log1p <= 2 ulp,
  * lgamma/betaln absolute error <= 2e-5 * max(1, |result|), erfinv <= 4e-7
  * relative away from +-1.
  */

@@ -5,7 +5,10 @@
  * Shaw, "Parallel random numbers: as easy as 1, 2, 3" (SC'11); rotation
  * constants {13,15,26,6} / {17,29,16,24}, key-schedule parity 0x1BD11BDA,
  * key injection after every four rounds.  Known-answer vectors from the
- * Random123 distribution are checked in tests/test_random_kat.py.
+ * Random123 distribution are checked in tests/test_oracle_pins.py
+ * (test_threefry2x32_known_answers; the split / fold_in layout below in
+ * test_split_matches_documented_jax_outputs and
+ * test_split_and_fold_in_counter_layout).
  *
  * The key layout follows jax.random with the partitionable threefry
  * implementation (the default of the jax version the reference pins):

@@ -1298,6 +1298,16 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
 
 std::atomic<uint64_t> g_tower_launches{0};
 
+// Optional timing of the convolutions: a pair of CUDA events around the
+// conv launches of each forward (recorded on the forward's stream), for a
+// caller that reports the convolutions' share and throughput inside a
+// longer step.  Off unless scacchi_tower_timing enabled it.
+struct ConvTiming {
+  cudaEvent_t *ev = nullptr;  // [2 * cap]
+  int cap = 0, used = 0;
+};
+ConvTiming g_conv_timing;
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -1496,6 +1506,8 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   // per layer: [terms == 3 ? 2 : 1][9 taps][128 out][128 in]
   const size_t conv_elems = (size_t)9 * kC * kC * (w->terms == 3 ? 2 : 1);
+  const int timed = g_conv_timing.used < g_conv_timing.cap ? g_conv_timing.used++ : -1;
+  if (timed >= 0) cudaEventRecord(g_conv_timing.ev[2 * timed], st);
   for (int blk = 0; blk < w->num_blocks; ++blk) {
     const uint16_t *w1 = w->conv_w + (size_t)(2 * blk) * conv_elems;
     const uint16_t *w2 = w->conv_w + (size_t)(2 * blk + 1) * conv_elems;
@@ -1519,6 +1531,7 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
     }
     if (rc) return rc;
   }
+  if (timed >= 0) cudaEventRecord(g_conv_timing.ev[2 * timed + 1], st);
   HeadWeights hw;
   hw.A = w->num_actions;
   hw.policy_w = w->policy_w;
@@ -1559,5 +1572,42 @@ int scacchi_tower_error(uint32_t *flags) {
 }
 
 uint64_t scacchi_tower_launch_count(void) { return g_tower_launches.load(std::memory_order_relaxed); }
+
+int scacchi_tower_timing(int32_t max_forwards) {
+  if (max_forwards < 0) return SCACCHI_EINVAL;
+  ConvTiming &t = g_conv_timing;
+  for (int i = 0; i < 2 * t.cap; ++i) cudaEventDestroy(t.ev[i]);
+  delete[] t.ev;
+  t = ConvTiming();
+  if (max_forwards == 0) return SCACCHI_OK;
+  t.ev = new cudaEvent_t[2 * (size_t)max_forwards];
+  for (int i = 0; i < 2 * max_forwards; ++i) {
+    if (cudaEventCreate(&t.ev[i]) != cudaSuccess) {
+      for (int j = 0; j < i; ++j) cudaEventDestroy(t.ev[j]);
+      delete[] t.ev;
+      t = ConvTiming();
+      return SCACCHI_ECUDA;
+    }
+  }
+  t.cap = max_forwards;
+  return SCACCHI_OK;
+}
+
+int scacchi_tower_timing_read(float *conv_ms, int32_t *forwards) {
+  if (!conv_ms || !forwards) return SCACCHI_EINVAL;
+  ConvTiming &t = g_conv_timing;
+  float total = 0.0f;
+  for (int i = 0; i < t.used; ++i) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(t.ev[2 * i + 1]) != cudaSuccess ||
+        cudaEventElapsedTime(&ms, t.ev[2 * i], t.ev[2 * i + 1]) != cudaSuccess)
+      return SCACCHI_ECUDA;
+    total += ms;
+  }
+  *conv_ms = total;
+  *forwards = t.used;
+  t.used = 0;
+  return SCACCHI_OK;
+}
 
 }  // extern "C"

@@ -21,6 +21,43 @@ from .posterior_updates import rule_params, update_posterior
 from .tree import Tree, _init_tree, ptr, stream_handle
 
 
+class PhaseTimer:
+    """CUDA events around the phases of the host-driven loop (simulate,
+    recurrent, expand, backward), recorded on the current stream; install
+    with ``set_phase_timer``.  Measurement only: the loop records nothing
+    when no timer is installed."""
+
+    PHASES = ("simulate", "recurrent", "expand", "backward")
+
+    def __init__(self):
+        self.marks = []
+
+    def mark(self) -> None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record(torch.cuda.current_stream())
+        self.marks.append(e)
+
+    def totals_ms(self) -> dict:
+        """Summed milliseconds per phase over every simulation timed so far."""
+        torch.cuda.synchronize()
+        out = {p: 0.0 for p in self.PHASES}
+        for i in range(0, len(self.marks) - 4, 5):
+            for j, p in enumerate(self.PHASES):
+                out[p] += self.marks[i + j].elapsed_time(self.marks[i + j + 1])
+        return out
+
+    def reset(self) -> None:
+        self.marks = []
+
+
+_PHASE_TIMER: PhaseTimer | None = None
+
+
+def set_phase_timer(timer: PhaseTimer | None) -> None:
+    global _PHASE_TIMER
+    _PHASE_TIMER = timer
+
+
 class SimulationBuffers:
     """Per-simulation device buffers: Simulation + recurrent outputs."""
 
@@ -111,13 +148,24 @@ def search(params: Any, rng_key, *, root: RootFnOutput, recurrent_fn: Callable,
         recurrent_fn.native_search(tree, keys, num_simulations, max_depth, rparams, stats)
         return tree
     bufs = SimulationBuffers(tree.batch, tree.A, tree.E, dev)
+    timer = _PHASE_TIMER
     for i in range(num_simulations):
+        if timer is not None:
+            timer.mark()
         simulate(tree, keys[i, 1], max_depth, bufs, None if stats is None else stats[4:])
+        if timer is not None:
+            timer.mark()
         embedding = tree.codec.unpack(bufs.parent_embedding[:, :tree.E]) if tree.codec is not None else None
         step, child = recurrent_fn(params, sched[i, 2], bufs.action, embedding)
         child_bytes = None
         if tree.codec is not None and tree.E:
             child_bytes = tree.codec.pack(child, tree.batch, dev)
+        if timer is not None:
+            timer.mark()
         v, tp = expand(tree, i + 1, bufs, step, child_bytes)
+        if timer is not None:
+            timer.mark()
         backward(tree, keys[i, 3], bufs, v, tp, rparams, stats)
+        if timer is not None:
+            timer.mark()
     return tree
