@@ -268,15 +268,17 @@ def full_step_bench(steps: int, warmup: int, precision: str | None, population: 
     state = game.random_roots(FULL_LANES, R.fold_in(R.PRNGKey(ROOT_SEED), rank), 0, 20)
     key = sharding.device_key(R.PRNGKey(SEARCH_SEED))
     stream = torch.cuda.current_stream(dev)
-    gather_ev = []
+    gather_ev = []  # per step: (step start, search done, gather done)
 
     def step(s):
+        s0 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
         t = search(s, key)
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record(stream)
         out = gather_targets(t, sharding)
         g1.record(stream)
-        gather_ev.append((g0, g1))
+        gather_ev.append((s0, g0, g1))
         return out
 
     for _ in range(warmup):
@@ -311,11 +313,16 @@ def full_step_bench(steps: int, warmup: int, precision: str | None, population: 
     phases = timer.totals_ms()
     _barrier(world)
     my_ms = e0.elapsed_time(e1) / steps
-    gather_ms = sum(a.elapsed_time(b) for a, b in gather_ev) / steps
+    # this rank's search alone (before the collective) and its all-gather
+    # (which includes waiting for the slowest rank's search)
+    search_ms = sum(a.elapsed_time(b) for a, b, _ in gather_ev) / steps
+    gather_ms = sum(b.elapsed_time(c) for _, b, c in gather_ev) / steps
     rank_ms = _all_ranks(my_ms, world)
+    rank_search = _all_ranks(search_ms, world)
+    rank_gather = _all_ranks(gather_ms, world)
     ms = max(rank_ms)
-    gather_max = _max_over_ranks(gather_ms, world)
-    out = {"ms_per_step": ms, "rank_ms": rank_ms, "gather_ms": gather_max, "launches_per_step": launches / steps,
+    out = {"ms_per_step": ms, "rank_ms": rank_ms, "rank_search_ms": rank_search, "rank_gather_ms": rank_gather,
+           "gather_ms": min(rank_gather), "launches_per_step": launches / steps,
            "conv_ms_per_step": conv_ms.value / steps, "forwards": forwards.value,
            "conv_launch_ms": conv_ms.value / max(forwards.value, 1) / 12,
            "phases_ms_per_step": {k: v / steps for k, v in phases.items()}, "precision": net.precision,
@@ -720,7 +727,7 @@ def cpu_fullstep_lanes(lo: int, hi: int, population: bool = False, threads: int 
     return hi - lo
 
 
-def cpu_baseline(population: bool, lanes: int = 4) -> dict:
+def cpu_baseline(population: bool, lanes: int = 16) -> dict:
     t0 = time.perf_counter()
     n = cpu_fullstep_lanes(0, lanes, population, threads=1)
     dt = time.perf_counter() - t0
@@ -889,8 +896,15 @@ def main() -> None:
                         "ms_per_step": round(f["e2e_ms"], 3)},
                 "gpu_launches": int(round(f["launches_per_step"] * args.steps)), "roofline": roof,
                 "ranks": {"ms_per_step": [round(v, 3) for v in f["rank_ms"]],
-                          "min": round(min(f["rank_ms"]), 3), "median": round(statistics.median(f["rank_ms"]), 3),
-                          "max": round(max(f["rank_ms"]), 3), "all_gather_ms": round(f["gather_ms"], 4)},
+                          "search_ms": [round(v, 3) for v in f["rank_search_ms"]],
+                          "search_min": round(min(f["rank_search_ms"]), 3),
+                          "search_median": round(statistics.median(f["rank_search_ms"]), 3),
+                          "search_max": round(max(f["rank_search_ms"]), 3),
+                          "gather_ms": [round(v, 4) for v in f["rank_gather_ms"]],
+                          "all_gather_ms": round(f["gather_ms"], 4),
+                          "note": "search_ms: each rank's search before the collective; gather_ms: its all-gather, "
+                                  "which includes waiting for the slowest rank; all_gather_ms: the smallest "
+                                  "(the collective itself)"},
                 **sub,
             }
             if world == 1 and not args.no_cpu_baseline:
