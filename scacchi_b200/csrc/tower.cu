@@ -571,27 +571,36 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
   const int mrow = lane & 7, mat = lane >> 3;
   const uint32_t lane_addr = acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)row_base;
   const int ch0 = quad * 32 + lane / 4;  // + 8 m: this thread's channels
-#pragma unroll 1
-  for (int jj = 0; jj < 4; ++jj) {
-    uint32_t d[2][2][4];  // [block of the two][lane group][fragment register]
+  // Software pipeline over the four 16-row steps jj: the accumulator
+  // columns and the residual of step jj + 1 are requested before step jj
+  // is computed, so their latency hides behind that step's arithmetic
+  // (tcgen05.wait::ld then only waits for loads issued a step earlier).
+  uint32_t d[2][2][2][4];  // [buffer][block of the two][lane group][fragment register]
+  float rx[2][2][4][2];    // [buffer][block][m][row of the pair]
+  auto request = [&](int jj, int buf) {
 #pragma unroll
     for (int j2 = 0; j2 < 2; ++j2)
 #pragma unroll
-      for (int g = 0; g < 2; ++g) tmem_ld16x256(lane_addr + ((uint32_t)(16 * g) << 16) + 8 * (2 * jj + j2), d[j2][g]);
-    // the residual's loads go out while the accumulator read is in flight
-    float rx[2][4][2];
+      for (int g = 0; g < 2; ++g)
+        tmem_ld16x256(lane_addr + ((uint32_t)(16 * g) << 16) + 8 * (2 * jj + j2), d[buf][j2][g]);
     if (conv2) {
 #pragma unroll
       for (int j2 = 0; j2 < 2; ++j2) {
         const size_t r0 = (size_t)tile * kBM + row_base + 8 * (2 * jj + j2) + 2 * (lane & 3);
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          rx[j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
-          rx[j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+          rx[buf][j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
+          rx[buf][j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
         }
       }
     }
+  };
+  request(0, 0);
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const int cur = jj & 1;
     tmem_wait_ld();
+    if (jj + 1 < 4) request(jj + 1, cur ^ 1);
 #pragma unroll
     for (int j2 = 0; j2 < 2; ++j2) {
       const int rb = row_base + 8 * (2 * jj + j2);  // first row of the 8-row block in the tile
@@ -602,15 +611,15 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const int g = m >> 1, hi = m & 1;
-        const float y0 = __uint_as_float(d[j2][g][2 * hi]) + cst[0][m];
-        const float y1 = __uint_as_float(d[j2][g][2 * hi + 1]) + cst[0][m];
+        const float y0 = __uint_as_float(d[cur][j2][g][2 * hi]) + cst[0][m];
+        const float y1 = __uint_as_float(d[cur][j2][g][2 * hi + 1]) + cst[0][m];
         float v0, v1;
         if (!conv2) {
           v0 = real0 ? fmaxf(y0, 0.0f) : 0.0f;
           v1 = real1 ? fmaxf(y1, 0.0f) : 0.0f;
         } else {
-          const float x0 = real0 ? y0 + rx[j2][m][0] : 0.0f;
-          const float x1 = real1 ? y1 + rx[j2][m][1] : 0.0f;
+          const float x0 = real0 ? y0 + rx[cur][j2][m][0] : 0.0f;
+          const float x1 = real1 ? y1 + rx[cur][j2][m][1] : 0.0f;
           ep.x32[(size_t)r0 * kC + ch0 + 8 * m] = x0;
           ep.x32[(size_t)(r0 + 1) * kC + ch0 + 8 * m] = x1;
           v0 = real0 ? fmaxf(fmaf(x0, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
