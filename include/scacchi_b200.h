@@ -277,7 +277,12 @@ int scacchi_search_synthetic(const scacchi_tree *tree, const scacchi_synthetic_p
  *     and 16-byte states the limit is 5,294 lanes.
  *   - The first call on a device resolves the array's device address with
  *     that device current (cudaGetSymbolAddress); make that first call
- *     before any stream capture on the device.
+ *     before any stream capture on the device.  The address is kept with
+ *     the context it was resolved in: after the context is torn down and
+ *     created again (cudaDeviceReset) the next call resolves it again, so
+ *     that call too belongs before any capture.
+ *   - A malformed descriptor returns SCACCHI_EINVAL before the size is
+ *     looked at.
  *   - All calls on a device share the one array, which keeps the last
  *     call's contents.  Calls whose work overlaps on the GPU (different
  *     streams, or different host threads without ordering) race on it and

@@ -17,11 +17,14 @@
 // rejected, and masked or categorical actions draw nothing.  The results are
 // the same as drawing the full [4, ..., A, O] arrays.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <atomic>
 #include <climits>
+#include <mutex>
 
 #include "../../include/scacchi_b200.h"
 #include "synthetic_env.h"
@@ -2245,8 +2248,30 @@ static __device__ __align__(256) uint8_t g_search_scratch[SCACCHI_STATIC_SCRATCH
 namespace {
 
 constexpr int kMaxScratchDevices = 64;
-// Device address of g_search_scratch per device, resolved on first use.
-std::atomic<void *> g_scratch_addr[kMaxScratchDevices];
+// Device address of g_search_scratch per device, resolved on first use in
+// the device's current context.  A context torn down and created again
+// (cudaDeviceReset, a primary-context reset) reloads the module at a new
+// address, so the address is kept together with the context it was
+// resolved in and resolved again when the current context differs.
+struct ScratchSlot {
+  CUcontext ctx = nullptr;
+  void *addr = nullptr;
+};
+ScratchSlot g_scratch_slot[kMaxScratchDevices];
+std::mutex g_scratch_mutex;
+
+PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  return fn;
+}
 
 }  // namespace
 
@@ -2255,18 +2280,34 @@ extern "C" {
 int scacchi_search_synthetic_static(const scacchi_tree *tree, const scacchi_synthetic_params *env,
                                     const uint32_t *keys, int32_t num_simulations, int32_t max_depth,
                                     const scacchi_update_params *params, uint64_t *stats, void *stream) {
-  if (!tree || tree->batch < 0 || tree->num_actions < 1) return SCACCHI_EINVAL;
+  // the descriptor first (a malformed call is EINVAL whatever its size),
+  // then the size against the array
+  if (!tree_ok(tree) || !env || !keys || num_simulations < 0 || max_depth < 1 || !params_ok(params) ||
+      env->num_actions != tree->num_actions || tree->emb_bytes != (int32_t)sizeof(se_state) ||
+      num_simulations + 1 > tree->num_nodes)
+    return SCACCHI_EINVAL;
   const size_t need = scacchi_search_workspace_bytes(tree->batch, tree->num_actions, tree->emb_bytes);
   if (need > (size_t)SCACCHI_STATIC_SCRATCH_BYTES) return SCACCHI_ETOOLARGE;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) return SCACCHI_ECUDA;
   if (dev < 0 || dev >= kMaxScratchDevices) return SCACCHI_ECUDA;
-  void *scratch = g_scratch_addr[dev].load(std::memory_order_acquire);
-  if (!scratch) {
-    // Set-up, once per device, with that device current.  Two threads that
-    // race here both store the same address.
-    if (cudaGetSymbolAddress(&scratch, g_search_scratch) != cudaSuccess || !scratch) return SCACCHI_ECUDA;
-    g_scratch_addr[dev].store(scratch, std::memory_order_release);
+  CUcontext ctx = nullptr;
+  auto get_ctx = ctx_get_current();
+  if (!get_ctx || get_ctx(&ctx) != CUDA_SUCCESS) return SCACCHI_ECUDA;
+  void *scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    ScratchSlot &slot = g_scratch_slot[dev];
+    if (!ctx || slot.ctx != ctx || !slot.addr) {
+      // Set-up, once per device and context, with that device current
+      // (the lookup also makes the runtime create the device's context if
+      // this thread has none yet).
+      if (cudaGetSymbolAddress(&scratch, g_search_scratch) != cudaSuccess || !scratch) return SCACCHI_ECUDA;
+      if (!ctx && (get_ctx(&ctx) != CUDA_SUCCESS || !ctx)) return SCACCHI_ECUDA;
+      slot.ctx = ctx;
+      slot.addr = scratch;
+    }
+    scratch = slot.addr;
   }
   // Every scratch byte a simulation reads is written earlier in the same
   // simulation (the descent writes parent, action, active and the parent

@@ -40,12 +40,24 @@ def _search(entry: str, B: int, N: int, seed: int, key_seed: int, prefix: bool):
                                           ptr(ws), ptr(stats), stream)
         held = 0
     else:
-        torch.cuda.synchronize()
-        free_before = torch.cuda.mem_get_info()[0]
-        rc = lib.scacchi_search_synthetic_static(tree.sref(), C.byref(game._params), ptr(keys), N, N,
-                                                 C.byref(rule), ptr(stats), stream)
-        torch.cuda.synchronize()
-        held = free_before - torch.cuda.mem_get_info()[0]
+        # device-wide free memory around the call: another process on a
+        # shared GPU can allocate in between, so the smallest of a few
+        # readings is what the call itself took
+        held = None
+        for _ in range(3):
+            torch.cuda.synchronize()
+            free_before = torch.cuda.mem_get_info()[0]
+            rc = lib.scacchi_search_synthetic_static(tree.sref(), C.byref(game._params), ptr(keys), N, N,
+                                                     C.byref(rule), ptr(stats), stream)
+            torch.cuda.synchronize()
+            took = free_before - torch.cuda.mem_get_info()[0]
+            held = took if held is None else min(held, took)
+            if rc != _lib.OK:
+                break
+            if _ < 2:
+                # the next reading reruns the same search on a fresh tree
+                tree = _init_tree(root, N, ~torch.isfinite(root.prior_logits), full=False)
+                stats.zero_()
     assert rc == _lib.OK
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
@@ -70,7 +82,7 @@ def test_static_scratch_matches_workspace_on_two_calls_in_a_row(cuda):
     small = dict(B=333, N=20, seed=4, key_seed=8, prefix=False)
     want = _search("workspace", **small)[0]
     got, held = _search("static", **small)
-    assert held <= 0  # the call itself took no device memory
+    assert held < 2 << 20  # the call itself took no device memory (allocations come in 2 MiB pages)
     _assert_same(got, want)
     assert got["stats"][0] > 0
 
@@ -87,11 +99,25 @@ def test_static_scratch_rejects_batches_beyond_its_size(cuda):
     while lib.scacchi_search_workspace_bytes(B + 1, A, E) <= limit:
         B += 1
     assert B == 5294
-    # a tree descriptor of B + 1 lanes is rejected before any pointer is read
-    tree = _lib.ScacchiTree()
-    tree.batch, tree.num_nodes, tree.num_actions, tree.action_stride, tree.emb_bytes = B + 1, 2, A, 96, E
-    params = SyntheticGameConfig().params()
-    keys = np.zeros(8, np.uint32)
-    rc = lib.scacchi_search_synthetic_static(C.byref(tree), C.byref(params), keys.ctypes.data_as(C.c_void_p), 1, 1,
-                                             C.byref(prefix_cdf_params()), None, None)
+    # a well-formed tree of B + 1 lanes is rejected before anything launches
+    from scacchi_b200 import random as R
+    from scacchi_b200.dirichlet_mctx.tree import _init_tree, ptr
+    from scacchi_b200.synthetic import SyntheticGame
+
+    game = SyntheticGame(SyntheticGameConfig(num_actions=A))
+    root = game.root(B + 1)
+    tree = _init_tree(root, 1, ~torch.isfinite(root.prior_logits), full=False)
+    keys = torch.from_numpy(R.key_schedule(R.PRNGKey(0), 1)).cuda()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    before = [getattr(tree, f).clone() for f in ("parents", "node_payload")]
+    rc = lib.scacchi_search_synthetic_static(tree.sref(), C.byref(game._params), ptr(keys), 1, 1,
+                                             C.byref(prefix_cdf_params()), None, stream)
     assert rc == _lib.ETOOLARGE
+    torch.cuda.synchronize()
+    assert all(torch.equal(a, getattr(tree, f)) for a, f in zip(before, ("parents", "node_payload")))
+    # a malformed descriptor of the same size is EINVAL, not ETOOLARGE
+    bad = _lib.ScacchiTree.from_buffer_copy(tree._struct)
+    bad.emb_bytes = 4
+    rc = lib.scacchi_search_synthetic_static(C.byref(bad), C.byref(game._params), ptr(keys), 1, 1,
+                                             C.byref(prefix_cdf_params()), None, stream)
+    assert rc == _lib.EINVAL
