@@ -431,6 +431,69 @@ uint64_t scacchi_tower_launch_count(void);
 int scacchi_tower_timing(int32_t max_forwards);
 int scacchi_tower_timing_read(float *conv_ms, int32_t *forwards);
 
+/* ---- the callers either side of the root: targets and loss input ------- */
+
+/* _run_dirichlet_thompson_search's target packing (play_search.py:490-548)
+ * with build_q_supervision (dirichlet_q_search.py:119-182), from the tree
+ * summary: per [batch, num_actions] q_kind (int8: 0 pad, 1 Dirichlet, 2
+ * categorical), selected, pair_weight, positive_evidence, positive_policy,
+ * q_weight; per lane v_kind, v_weight and the search loss mask (sum of the
+ * policy target > 0).  action_set 0 = positive search evidence or solved, 1
+ * = positive posterior policy or solved; reduction 0 = mean over selected
+ * pairs, 1 = legacy source-weighted.  Booleans are one byte. */
+int scacchi_pack_targets(int32_t batch, int32_t num_actions, const float *visit_counts, const float *policy_target,
+                         const uint8_t *legal, const int8_t *q_outcome, const int8_t *v_outcome, int32_t action_set,
+                         int32_t reduction, int8_t *q_kind, int8_t *v_kind, uint8_t *mask, uint8_t *selected,
+                         float *pair_weight, uint8_t *positive_evidence, uint8_t *positive_policy, float *q_weight,
+                         float *v_weight, void *stream);
+
+/* Self-play frames of `batch` trajectories x `frames_per_lane` steps, lane
+ * major ([B, T] and [B, T, A]), as compute_loss_input reads them
+ * (loss.py:164-357).  search_mask may be NULL (then sum of the policy > 0). */
+typedef struct {
+  const float *reward, *discount;      /* [B, T] */
+  const uint8_t *terminated;           /* [B, T] */
+  const int32_t *played_action;        /* [B, T] */
+  const uint8_t *legal;                /* [B, T, A] */
+  const float *policy;                 /* [B, T, A] posterior policy target */
+  const uint8_t *search_mask;          /* [B, T] metadata mask, or NULL */
+  const uint8_t *q_pair_mask;          /* [B, T, A] q_supervision.selected */
+  const float *q_pair_weight;          /* [B, T, A] */
+  const int8_t *q_kind, *q_outcome;    /* [B, T, A] native Q sidecars */
+  const float *q_weight;
+  const int32_t *q_distance;
+  const int8_t *v_kind, *v_outcome;    /* [B, T] native V sidecars */
+  const float *v_weight;
+  const int32_t *v_distance;
+} scacchi_loss_frames;
+
+typedef struct {
+  float *value_tgt;                    /* [B, T] trajectory value targets */
+  uint8_t *value_mask, *policy_loss_mask, *value_loss_mask, *search_loss_mask;  /* [B, T] */
+  float *policy_tgt;                   /* [B, T, A] */
+  uint8_t *q_pair_mask;                /* [B, T, A] */
+  float *q_pair_weight;
+  int8_t *q_kind, *q_outcome;
+  float *q_weight;
+  int32_t *q_distance;
+  int8_t *v_kind, *v_outcome;          /* [B, T] */
+  float *v_weight;
+  int32_t *v_distance;
+} scacchi_loss_out;
+
+/* The frame-wise part of compute_loss_input: the reverse value scan
+ * (loss.py:231-245), the value / policy / value-loss / search-loss masks
+ * of loss_mask_mode (0 search, 1 value, 2 pgx), the winner-action policy
+ * target, and the exact one-step terminal targets (loss.py:117-136) on the
+ * played edge (terminal_edge_targets) and on a won terminal parent
+ * (terminal_parent_targets); legacy_reduction selects the legacy
+ * source-weighted Q pair weight.  One CTA per trajectory. */
+int scacchi_loss_input(const scacchi_loss_frames *frames, const scacchi_loss_out *out, int32_t batch,
+                       int32_t frames_per_lane, int32_t num_actions, int32_t num_outcomes, int32_t loss_mask_mode,
+                       int32_t winner_action_policy, int32_t terminal_edge_targets, int32_t terminal_parent_targets,
+                       int32_t legacy_reduction, void *stream);
+uint64_t scacchi_target_launch_count(void);
+
 /* ---- host-side jax.random key helpers (no device work) ---------------- */
 
 /* search.py:207-209 key chain: for i < num_simulations,

@@ -562,12 +562,14 @@ def root_readout(native, summary: dict, legal, *, search_evidence: bool, tempera
 TARGET_PAD, TARGET_DIRICHLET, TARGET_CATEGORICAL = 0, 1, 2
 
 
-def pack_targets(summary: dict, policy_target, legal, search_action) -> dict:
+def pack_targets(summary: dict, policy_target, legal, search_action, action_set: int = 0,
+                 reduction: int = 0) -> dict:
     """play_search.py:490-548 (_run_dirichlet_thompson_search's target
-    packing) with dirichlet_q_search.py:119-182 (build_q_supervision) for
-    the default QSupervisionConfig (positive search evidence or solved;
-    mean over selected state-action pairs).  numpy in, numpy out; keys are
-    the PosteriorTargets field names."""
+    packing) with dirichlet_q_search.py:119-182 (build_q_supervision).
+    action_set 0: positive search evidence or solved, 1: positive posterior
+    policy or solved; reduction 0: mean over selected state-action pairs,
+    1: legacy source-weighted.  numpy in, numpy out; keys are the
+    PosteriorTargets field names."""
     legal = np.asarray(legal, bool)
     policy_target = np.asarray(policy_target, np.float32)
     q_count = summary["visit_counts"][..., None]
@@ -576,11 +578,20 @@ def pack_targets(summary: dict, policy_target, legal, search_action) -> dict:
     q_kind = np.where(legal, np.where(q_cat, TARGET_CATEGORICAL, TARGET_DIRICHLET), TARGET_PAD).astype(np.int8)
     v_kind = np.where(v_cat, TARGET_CATEGORICAL, TARGET_DIRICHLET).astype(np.int8)
     positive_evidence = q_count.sum(-1) > 0
-    selected = legal & (positive_evidence | q_cat)
+    evidence_mass = (q_count.sum(-1) + np.zeros_like(policy_target)).astype(np.float32)
+    source_selected, source_weight = ((positive_evidence, evidence_mass) if action_set == 0 else
+                                      (policy_target > 0, policy_target))
+    selected = legal & (source_selected | q_cat)
+    if reduction == 0:
+        pair_weight = selected.astype(np.float32)
+    else:
+        with np.errstate(invalid="ignore"):
+            pair_weight = np.where(legal & q_cat, np.maximum(source_weight, np.float32(1.0)), source_weight)
+        pair_weight = np.where(selected, pair_weight, np.float32(0.0)).astype(np.float32)
     return dict(
         policy=policy_target, alpha_q=summary["alpha"], alpha_v=summary["value_alpha"],
         mask=policy_target.sum(-1) > 0, q_supervision_selected=selected,
-        q_supervision_pair_weight=selected.astype(np.float32),
+        q_supervision_pair_weight=pair_weight,
         q_positive_evidence_action=legal & positive_evidence, q_positive_policy_action=legal & (policy_target > 0),
         search_action=np.asarray(search_action, np.int32), q_target_kind=q_kind,
         q_target_weight=legal.astype(np.float32), q_target_outcome=summary["q_categorical_outcome"],

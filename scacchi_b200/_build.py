@@ -14,7 +14,7 @@ LIB = os.path.join(HERE, "libscacchi_b200.so")
 # explicitly where they want one).  The network kernels are checked to a
 # tolerance and keep contraction.
 UNITS = [(os.path.join(CSRC, "search.cu"), ["-fmad=false"]), (os.path.join(CSRC, "tower.cu"), []),
-         (os.path.join(CSRC, "hex.cu"), ["-fmad=false"])]
+         (os.path.join(CSRC, "hex.cu"), ["-fmad=false"]), (os.path.join(CSRC, "targets.cu"), ["-fmad=false"])]
 SOURCES = [u[0] for u in UNITS]
 HEADERS = [os.path.join(CSRC, h) for h in ("smath.h", "threefry.h", "synthetic_env.h", "lane_cta.cuh")] + [
     os.path.join(ROOT, "include", "scacchi_b200.h")]

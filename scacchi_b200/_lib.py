@@ -59,6 +59,20 @@ class TowerWeights(C.Structure):
         (n, C.c_void_p) for n in POINTERS]
 
 
+class LossFrames(C.Structure):
+    FIELDS = ("reward", "discount", "terminated", "played_action", "legal", "policy", "search_mask", "q_pair_mask",
+              "q_pair_weight", "q_kind", "q_outcome", "q_weight", "q_distance", "v_kind", "v_outcome", "v_weight",
+              "v_distance")
+    _fields_ = [(n, C.c_void_p) for n in FIELDS]
+
+
+class LossOut(C.Structure):
+    FIELDS = ("value_tgt", "value_mask", "policy_loss_mask", "value_loss_mask", "search_loss_mask", "policy_tgt",
+              "q_pair_mask", "q_pair_weight", "q_kind", "q_outcome", "q_weight", "q_distance", "v_kind", "v_outcome",
+              "v_weight", "v_distance")
+    _fields_ = [(n, C.c_void_p) for n in FIELDS]
+
+
 P = C.c_void_p
 I32 = C.c_int32
 F32 = C.c_float
@@ -103,13 +117,17 @@ SIGNATURES = {
     "scacchi_tower_error": [P],
     "scacchi_tower_launch_count": [],
     "scacchi_tower_timing": [I32],
+    "scacchi_pack_targets": [I32, I32, P, P, P, P, P, I32, I32, P, P, P, P, P, P, P, P, P, P],
+    "scacchi_loss_input": [C.POINTER(LossFrames), C.POINTER(LossOut), I32, I32, I32, I32, I32, I32, I32, I32, I32, P],
+    "scacchi_target_launch_count": [],
     "scacchi_tower_timing_read": [P, P],
     "scacchi_device_error": [P],
     "scacchi_launch_count": [],
 }
 RESTYPES = {"scacchi_search_workspace_bytes": C.c_size_t, "scacchi_launch_count": C.c_uint64,
             "scacchi_tower_rows": C.c_uint64, "scacchi_tower_workspace_bytes": C.c_size_t,
-            "scacchi_tower_launch_count": C.c_uint64, "scacchi_hex_launch_count": C.c_uint64}
+            "scacchi_tower_launch_count": C.c_uint64, "scacchi_hex_launch_count": C.c_uint64,
+            "scacchi_target_launch_count": C.c_uint64}
 
 
 class ScacchiError(RuntimeError):
@@ -152,7 +170,7 @@ def device_error() -> int:
 def launch_count() -> int:
     """Kernels this library launched since load (search + network + Hex)."""
     return (int(lib().scacchi_launch_count()) + int(lib().scacchi_tower_launch_count())
-            + int(lib().scacchi_hex_launch_count()))
+            + int(lib().scacchi_hex_launch_count()) + int(lib().scacchi_target_launch_count()))
 
 
 def tower_error() -> int:

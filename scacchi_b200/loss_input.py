@@ -3,22 +3,27 @@
 
 ``make_compute_input_for_lossfn(losses, num_outcomes)`` turns the
 batch-major TrainingSamples of ``play.play_training`` into the ``Sample``
-the losses read: trajectory value targets (a reverse discounted scan),
-the value/policy/search loss masks of each loss-mask mode, the winner-action
-policy target, and the optional exact one-step terminal targets, all as
-device tensor operations.
+the losses read.  The frame-wise work -- trajectory value targets (a
+reverse discounted scan), the value / policy / search loss masks of each
+loss-mask mode, the winner-action policy target and the optional exact
+one-step terminal targets -- is one CUDA kernel (scacchi_loss_input); this
+module fills the sidecars a posterior without metadata lacks and binds the
+kernel's outputs into the Sample.
 """
 
 from __future__ import annotations
 
+import ctypes as C
 import dataclasses
 from enum import StrEnum
 from typing import NamedTuple
 
 import torch
 
+from . import _lib
 from .dirichlet_mctx.outcomes import NO_OUTCOME
-from .play_search import TARGET_CATEGORICAL, TARGET_DIRICHLET
+from .dirichlet_mctx.tree import ptr, stream_handle
+from .play_search import TARGET_DIRICHLET
 from .types import QPairReduction, QSupervisionConfig
 
 NO_DISTANCE = -1
@@ -100,27 +105,6 @@ def _native_target_fields(metadata, beta_q, beta_v) -> dict:
     return values
 
 
-def _with_categorical_targets(targets: dict, head: str, mask: torch.Tensor, outcome: torch.Tensor) -> dict:
-    """loss.py:117-136: exact one-step outcomes on the masked entries."""
-    updated = dict(targets)
-    for field, value in (("kind", TARGET_CATEGORICAL), ("weight", 1), ("outcome", outcome), ("distance", 1)):
-        name = f"{head}_target_{field}"
-        prev = updated[name]
-        val = value if isinstance(value, torch.Tensor) else torch.tensor(value, device=prev.device)
-        updated[name] = torch.where(mask, val.to(prev.dtype), prev)
-    return updated
-
-
-def _outcome_index(value_tgt: torch.Tensor, num_outcomes: int) -> torch.Tensor:
-    """loss.py:511-517."""
-    rounded = torch.round(value_tgt).to(torch.int32)
-    if num_outcomes == 2:
-        return torch.div(rounded + 1, 2, rounding_mode="floor")
-    if num_outcomes == 3:
-        return rounded + 1
-    raise ValueError(f"unsupported outcome count: {num_outcomes}")
-
-
 def _empty_posterior_targets(policy: torch.Tensor, num_outcomes: int):
     """loss.py:139-161."""
     q_pair_weight = policy * 0.0
@@ -130,19 +114,9 @@ def _empty_posterior_targets(policy: torch.Tensor, num_outcomes: int):
     return beta_q, beta_v, mask, q_pair_weight
 
 
-def trajectory_value_targets(reward: torch.Tensor, discount: torch.Tensor) -> torch.Tensor:
-    """loss.py:231-245: v_t = r_t + d_t * v_{t+1}, scanned from the end of
-    each [B, T] trajectory."""
-    values = torch.empty_like(reward)
-    carry = torch.zeros_like(reward[:, 0])
-    for t in range(reward.shape[1] - 1, -1, -1):
-        carry = reward[:, t] + discount[:, t] * carry
-        values[:, t] = carry
-    return values
-
-
 def make_compute_input_for_lossfn(losses: TrainingLossConfig, num_outcomes: int = 2):
-    """loss.py:164-357."""
+    """loss.py:164-357 (frames on a CUDA device)."""
+    mask_modes = {LossMaskMode.search: 0, LossMaskMode.value: 1, LossMaskMode.pgx: 2}
 
     def compute_loss_input(source) -> Sample:
         prediction = source.posterior.prediction
@@ -152,6 +126,8 @@ def make_compute_input_for_lossfn(losses: TrainingLossConfig, num_outcomes: int 
             return None if metadata is None else getattr(metadata, field, None)
 
         policy = prediction.policy
+        if policy.device.type != "cuda":
+            raise ValueError("the loss input is assembled on the GPU: pass frames on a CUDA device")
         beta_q, beta_v = prediction.alpha_q, prediction.alpha_v
         q_supervision = metadata_value("q_supervision")
         if beta_q is None or beta_v is None or q_supervision is None:
@@ -164,51 +140,63 @@ def make_compute_input_for_lossfn(losses: TrainingLossConfig, num_outcomes: int 
         positive_policy = metadata_value("q_positive_policy_action")
         if positive_policy is None:
             positive_policy = torch.zeros_like(policy, dtype=torch.bool)
-
-        # a frame counts for the value once its trajectory ends inside the window
-        value_mask = torch.flip(torch.cumsum(torch.flip(source.terminated.to(torch.int32), [1]), 1), [1]) >= 1
-        legal_policy_mask = source.legal_action_mask.any(-1)
-        metadata_mask = metadata_value("mask")
-        search_loss_mask = metadata_mask if metadata_mask is not None else policy.sum(-1) > 0
-        value_tgt = trajectory_value_targets(source.reward, source.discount)
-        policy_tgt = policy
-        policy_loss_mask = legal_policy_mask & search_loss_mask
-        value_loss_mask = search_loss_mask
-        mode = LossMaskMode(losses.loss_mask_mode)
-        if mode == LossMaskMode.value:
-            policy_loss_mask = value_mask
-            value_loss_mask = value_mask
-        elif mode == LossMaskMode.pgx:
-            value_loss_mask = value_mask
-        if PolicyTargetMode(losses.policy_target_mode) == PolicyTargetMode.winner_action:
-            policy_tgt = torch.nn.functional.one_hot(source.played_action.long(), policy.shape[-1]).to(policy.dtype)
-            policy_loss_mask = legal_policy_mask & value_mask & (value_tgt > 0)
-
         native = _native_target_fields(metadata, beta_q, beta_v)
-        if losses.terminal_edge_targets or losses.terminal_parent_targets:
-            outcome_index = _outcome_index(source.reward, beta_v.shape[-1])
-            played = torch.nn.functional.one_hot(source.played_action.long(), beta_q.shape[-2]).to(torch.bool)
-            terminal_action_mask = source.terminated[..., None] & played
-        if losses.terminal_edge_targets:
-            native = _with_categorical_targets(native, "q", terminal_action_mask, outcome_index[..., None])
-            q_pair_mask = q_pair_mask | terminal_action_mask
-            if losses.q_supervision.reduction == QPairReduction.legacy_normalized_source_weighted_mean:
-                terminal_weight = torch.clamp(q_pair_weight, min=1.0)
-            else:
-                terminal_weight = torch.ones_like(q_pair_weight)
-            q_pair_weight = torch.where(terminal_action_mask, terminal_weight, q_pair_weight)
-        if losses.terminal_parent_targets:
-            win = source.terminated & (source.reward > 0)
-            policy_tgt = torch.where(win[..., None], played.to(policy_tgt.dtype), policy_tgt)
-            policy_loss_mask = policy_loss_mask | (win & legal_policy_mask)
-            value_loss_mask = value_loss_mask | win
-            native = _with_categorical_targets(native, "v", win, outcome_index)
+        B, T, A = policy.shape
+        dev = policy.device
+        # the terminal targets take the outcome count from beta_V (the
+        # outcome index is only read with them; 2 stands in otherwise)
+        terminal = losses.terminal_edge_targets or losses.terminal_parent_targets
+        outcomes = beta_v.shape[-1] if terminal else 2
+        if outcomes not in (2, 3):
+            raise ValueError(f"unsupported outcome count: {outcomes}")
 
-        return Sample(obs=source.obs, policy_tgt=policy_tgt, value_tgt=value_tgt, played_action=source.played_action,
-                      policy_mask=source.legal_action_mask, value_mask=value_mask, beta_Q_target=beta_q,
-                      beta_V_target=beta_v, q_supervised_pair_mask=q_pair_mask, q_pair_weight=q_pair_weight,
-                      q_positive_evidence_action_mask=evidence, q_positive_policy_action_mask=positive_policy,
-                      policy_loss_mask=policy_loss_mask, value_loss_mask=value_loss_mask,
-                      search_loss_mask=search_loss_mask, outcome_mask=value_mask, **native)
+        def c(t, dtype):
+            return t.to(device=dev, dtype=dtype).contiguous()
+
+        f32, u8, i8, i32 = torch.float32, torch.uint8, torch.int8, torch.int32
+        ins = dict(reward=c(source.reward, f32), discount=c(source.discount, f32),
+                   terminated=c(source.terminated, u8), played_action=c(source.played_action, i32),
+                   legal=c(source.legal_action_mask, u8), policy=c(policy, f32),
+                   search_mask=None if metadata_value("mask") is None else c(metadata_value("mask"), u8),
+                   q_pair_mask=c(q_pair_mask.expand(B, T, A), u8), q_pair_weight=c(q_pair_weight.expand(B, T, A), f32),
+                   q_kind=c(native["q_target_kind"], i8), q_outcome=c(native["q_target_outcome"], i8),
+                   q_weight=c(native["q_target_weight"], f32), q_distance=c(native["q_target_distance"], i32),
+                   v_kind=c(native["v_target_kind"], i8), v_outcome=c(native["v_target_outcome"], i8),
+                   v_weight=c(native["v_target_weight"], f32), v_distance=c(native["v_target_distance"], i32))
+        outs = dict(value_tgt=torch.empty((B, T), dtype=f32, device=dev),
+                    value_mask=torch.empty((B, T), dtype=u8, device=dev),
+                    policy_loss_mask=torch.empty((B, T), dtype=u8, device=dev),
+                    value_loss_mask=torch.empty((B, T), dtype=u8, device=dev),
+                    search_loss_mask=torch.empty((B, T), dtype=u8, device=dev),
+                    policy_tgt=torch.empty((B, T, A), dtype=f32, device=dev),
+                    q_pair_mask=torch.empty((B, T, A), dtype=u8, device=dev),
+                    q_pair_weight=torch.empty((B, T, A), dtype=f32, device=dev),
+                    q_kind=torch.empty((B, T, A), dtype=i8, device=dev),
+                    q_outcome=torch.empty((B, T, A), dtype=i8, device=dev),
+                    q_weight=torch.empty((B, T, A), dtype=f32, device=dev),
+                    q_distance=torch.empty((B, T, A), dtype=i32, device=dev),
+                    v_kind=torch.empty((B, T), dtype=i8, device=dev), v_outcome=torch.empty((B, T), dtype=i8, device=dev),
+                    v_weight=torch.empty((B, T), dtype=f32, device=dev),
+                    v_distance=torch.empty((B, T), dtype=i32, device=dev))
+        frames = _lib.LossFrames(*[ptr(ins[k]) for k in _lib.LossFrames.FIELDS])
+        out = _lib.LossOut(*[ptr(outs[k]) for k in _lib.LossOut.FIELDS])
+        legacy = losses.q_supervision.reduction == QPairReduction.legacy_normalized_source_weighted_mean
+        _lib.check(_lib.lib().scacchi_loss_input(
+            C.byref(frames), C.byref(out), B, T, A, outcomes, mask_modes[LossMaskMode(losses.loss_mask_mode)],
+            int(PolicyTargetMode(losses.policy_target_mode) == PolicyTargetMode.winner_action),
+            int(losses.terminal_edge_targets), int(losses.terminal_parent_targets), int(legacy),
+            stream_handle(dev)), "loss_input")
+        value_mask = outs["value_mask"].bool()
+        return Sample(obs=source.obs, policy_tgt=outs["policy_tgt"], value_tgt=outs["value_tgt"],
+                      played_action=source.played_action, policy_mask=source.legal_action_mask, value_mask=value_mask,
+                      beta_Q_target=beta_q, beta_V_target=beta_v, q_supervised_pair_mask=outs["q_pair_mask"].bool(),
+                      q_pair_weight=outs["q_pair_weight"], q_positive_evidence_action_mask=evidence,
+                      q_positive_policy_action_mask=positive_policy,
+                      policy_loss_mask=outs["policy_loss_mask"].bool(), value_loss_mask=outs["value_loss_mask"].bool(),
+                      search_loss_mask=outs["search_loss_mask"].bool(), outcome_mask=value_mask,
+                      q_target_kind=outs["q_kind"], q_target_weight=outs["q_weight"],
+                      q_target_outcome=outs["q_outcome"], q_target_distance=outs["q_distance"],
+                      v_target_kind=outs["v_kind"], v_target_weight=outs["v_weight"],
+                      v_target_outcome=outs["v_outcome"], v_target_distance=outs["v_distance"])
 
     return compute_loss_input

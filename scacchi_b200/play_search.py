@@ -237,27 +237,50 @@ def run_dirichlet_thompson_search(env_state, prediction: EvaluatorOutput, expand
         record["policy_output"] = out
     summary = out.search_tree.summary()
     policy_target = dirichlet_root_policy_readout(out.action_weights, summary, legal, search_cfg)
-    beta_q, beta_v = summary.alpha, summary.value_alpha
-    q_count = summary.visit_counts[..., None]
-    q_cat = summary.q_categorical_outcome != NO_OUTCOME
-    v_cat = summary.v_categorical_outcome != NO_OUTCOME
-    i8 = dict(dtype=torch.int8, device=dev)
-    q_kind = torch.where(legal, torch.where(q_cat, torch.full_like(q_cat, TARGET_CATEGORICAL, **i8),
-                                            torch.full_like(q_cat, TARGET_DIRICHLET, **i8)),
-                         torch.full_like(q_cat, TARGET_PAD, **i8))
-    v_kind = torch.where(v_cat, torch.full_like(v_cat, TARGET_CATEGORICAL, **i8),
-                         torch.full_like(v_cat, TARGET_DIRICHLET, **i8))
-    q_sup = build_q_supervision(q_supervision_config.action_set, q_supervision_config.reduction, q_count,
-                                policy_target, q_cat, legal)
-    metadata = TargetMetadata(
-        mask=policy_target.sum(-1) > 0, q_supervision=q_sup,
-        q_positive_evidence_action=legal & (q_count.sum(-1) > 0), q_positive_policy_action=legal & (policy_target > 0),
-        search_action=out.action, q_target_kind=q_kind, q_target_weight=legal.to(beta_q.dtype),
+    metadata = pack_targets(summary, policy_target, legal, out.action, q_supervision_config)
+    return PosteriorTargets(prediction=PosteriorPrediction(policy=policy_target, alpha_v=summary.value_alpha,
+                                                           alpha_q=summary.alpha), metadata=metadata)
+
+
+def pack_targets(summary, policy_target: torch.Tensor, legal: torch.Tensor, search_action: torch.Tensor,
+                 q_supervision_config: QSupervisionConfig) -> TargetMetadata:
+    """play_search.py:490-548 with build_q_supervision
+    (dirichlet_q_search.py:119-182): the search's target metadata from the
+    tree summary, in one kernel (scacchi_pack_targets).  beta_Q / beta_V,
+    the categorical outcomes and distances are the summary's own tensors."""
+    action_sets = {QActionSet.positive_search_evidence_or_solved: 0, QActionSet.positive_posterior_policy_or_solved: 1}
+    reductions = {QPairReduction.mean_over_selected_state_action_pairs: 0,
+                  QPairReduction.legacy_normalized_source_weighted_mean: 1}
+    if q_supervision_config.action_set not in action_sets:
+        raise ValueError(f"unknown Q action set: {q_supervision_config.action_set!r}")
+    if q_supervision_config.reduction not in reductions:
+        raise ValueError(f"unknown Q pair reduction: {q_supervision_config.reduction!r}")
+    B, A = policy_target.shape
+    dev = policy_target.device
+    i8, u8, f32 = torch.int8, torch.uint8, torch.float32
+    q_kind = torch.empty((B, A), dtype=i8, device=dev)
+    v_kind = torch.empty((B,), dtype=i8, device=dev)
+    mask = torch.empty((B,), dtype=u8, device=dev)
+    selected = torch.empty((B, A), dtype=u8, device=dev)
+    pair_weight = torch.empty((B, A), dtype=f32, device=dev)
+    pos_evidence = torch.empty((B, A), dtype=u8, device=dev)
+    pos_policy = torch.empty((B, A), dtype=u8, device=dev)
+    q_weight = torch.empty((B, A), dtype=f32, device=dev)
+    v_weight = torch.empty((B,), dtype=f32, device=dev)
+    legal_u8 = legal.to(u8).contiguous()
+    _lib.check(_lib.lib().scacchi_pack_targets(
+        B, A, ptr(summary.visit_counts), ptr(policy_target.contiguous()), ptr(legal_u8),
+        ptr(summary.q_categorical_outcome), ptr(summary.v_categorical_outcome),
+        action_sets[q_supervision_config.action_set], reductions[q_supervision_config.reduction], ptr(q_kind),
+        ptr(v_kind), ptr(mask), ptr(selected), ptr(pair_weight), ptr(pos_evidence), ptr(pos_policy), ptr(q_weight),
+        ptr(v_weight), stream_handle(dev)), "pack_targets")
+    return TargetMetadata(
+        mask=mask.bool(), q_supervision=QSupervision(selected=selected.bool(), pair_weight=pair_weight),
+        q_positive_evidence_action=pos_evidence.bool(), q_positive_policy_action=pos_policy.bool(),
+        search_action=search_action, q_target_kind=q_kind, q_target_weight=q_weight,
         q_target_outcome=summary.q_categorical_outcome, q_target_distance=summary.q_categorical_distance,
-        v_target_kind=v_kind, v_target_weight=torch.ones_like(summary.v_categorical_distance, dtype=beta_v.dtype),
-        v_target_outcome=summary.v_categorical_outcome, v_target_distance=summary.v_categorical_distance)
-    return PosteriorTargets(prediction=PosteriorPrediction(policy=policy_target, alpha_v=beta_v, alpha_q=beta_q),
-                            metadata=metadata)
+        v_target_kind=v_kind, v_target_weight=v_weight, v_target_outcome=summary.v_categorical_outcome,
+        v_target_distance=summary.v_categorical_distance)
 
 
 def make_search(env, evaluator: Callable, search_cfg: SearchConfig | DirichletThompsonSearchConfig,

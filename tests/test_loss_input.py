@@ -1,9 +1,12 @@
-"""Loss-input assembly (scacchi/loss.py:164-357) on CPU tensors: the
-reference's assertions of tests/test_loss_masks.py:132-434."""
+"""The loss-input restatement (oracle/loss_ref.py, the checker of the
+scacchi_loss_input kernel; scacchi/loss.py:164-357) on CPU tensors, held to
+the reference's assertions of tests/test_loss_masks.py:132-434.  The same
+assertions run through the kernel in tests/test_gpu_targets.py."""
 
 import torch
 
-from scacchi_b200.loss_input import TrainingLossConfig, make_compute_input_for_lossfn, trajectory_value_targets
+from oracle.loss_ref import make_compute_input_for_lossfn, trajectory_value_targets
+from scacchi_b200.loss_input import TrainingLossConfig
 from scacchi_b200.play import TrainingSamples
 from scacchi_b200.play_search import (TARGET_CATEGORICAL, TARGET_DIRICHLET, PosteriorPrediction, PosteriorTargets,
                                       QSupervision, TargetMetadata)
