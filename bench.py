@@ -76,15 +76,17 @@ def source_hash(names) -> str:
 # while the sources still hash to its stamp; after a kernel change it prints
 # null with "stale" until the figure is captured again.
 CAPTURED = {
-    # dram__bytes_read.sum + dram__bytes_write.sum of backward launch 65 of the
-    # isolated-search warm-up step (profiles/backward_cta_search4096x128.md)
-    "backward_traffic_bytes": dict(value=23654656 + 3840, sources=SEARCH_SOURCES, sha="59bcc2b5b0892acc"),
-    # smsp__inst_executed.sum over the 128 backward launches of one
-    # isolated-search step (same profile)
-    "backward_warp_inst_per_step": dict(value=25875513797, sources=SEARCH_SOURCES, sha="59bcc2b5b0892acc"),
+    # dram__bytes_read.sum + dram__bytes_write.sum of one backward launch
+    # (simulation 64 of the isolated-search profile step;
+    # profiles/backward_cta_search4096x128.md)
+    "backward_traffic_bytes": dict(value=23669760 + 1024, sources=SEARCH_SOURCES, sha="718be44c55403747"),
+    # smsp__inst_executed.sum of that launch x 128 launches per step (an
+    # all-launch capture of an earlier build gave 5 % less: the middle
+    # simulation's paths are a little deeper than the step's average)
+    "backward_warp_inst_per_step": dict(value=212923824 * 128, sources=SEARCH_SOURCES, sha="718be44c55403747"),
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
-    "conv_traffic_bytes_8192": dict(value=1299666965, sources=TOWER_SOURCES, sha="a77c704a33eaa98e"),
+    "conv_traffic_bytes_8192": dict(value=1296633451, sources=TOWER_SOURCES, sha="1f6ba39481e23680"),
 }
 
 
