@@ -279,3 +279,33 @@ def test_other_precisions_against_fp32(cuda, tower_workload, precision):
     bound, min_agree = {"bf16": (0.4, 0.95), "fp16": (0.045, 0.99), "fp16x2": (2e-2, 0.995),
                         "fp16x3": (2e-3, 0.999)}[precision]
     assert max(err) < bound and agree >= min_agree
+
+
+@pytest.mark.parametrize("boards", [1, 2, 37, 1281])
+def test_ragged_board_counts_match_emulation(cuda, boards):
+    """Board counts whose padded rows end inside a tile (the last tile's
+    rows past the boards are padding) and tiny batches: the default
+    precision against the emulation of its rounding points, and the same
+    outputs when the boards are evaluated inside a larger batch."""
+    from oracle import network_ref as R
+    from scacchi_b200.network import DEFAULT_PRECISION, init_params
+
+    params = init_params(3, random_batchnorm=True, block_gain=0.5)
+    obs = R.observations(boards + 5, seed=boards)
+    got = _tower_outputs(params, obs[:boards], DEFAULT_PRECISION)
+    want = R.forward(params, obs[:boards], precision=DEFAULT_PRECISION)
+    for g, w in zip(got[:3], want):
+        assert np.abs(g - w).max() < EMULATION_TOL[DEFAULT_PRECISION]
+    more = _tower_outputs(params, obs, DEFAULT_PRECISION)
+    for g, m in zip(got, more):
+        np.testing.assert_allclose(g, m[:boards], rtol=2e-6, atol=2e-6)
+
+
+def test_forward_is_deterministic(cuda, tower_workload):
+    """Two forwards of the same boards give the same bits (no atomics in
+    the reductions)."""
+    params, obs, _ = tower_workload
+    a = _tower_outputs(params, obs[:2048], None)
+    b = _tower_outputs(params, obs[:2048], None)
+    for x, y in zip(a, b):
+        assert np.array_equal(x, y)
