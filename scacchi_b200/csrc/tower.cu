@@ -23,26 +23,25 @@
 //               as soon as the MMAs finish reading half h of this one
 //   warp 1      TMEM allocator and MMA issuer (one thread):
 //               tcgen05.mma.cta_group::1.kind::f16, K = 16, 16-bit
-//               operands -> fp32 in TMEM.  The residual layers run
-//               transposed: M = 128 output channels (A = the weight tile),
-//               N = 256 rows of the pair (B = the window from row 16 +
-//               shift; any row: the swizzle phase follows the address), so
-//               TMEM lane = channel and column = row, and a pair takes half
-//               the MMA instructions of two M = N = 128 products (the
-//               issue rate of those bounded the kernel).  The last layer
-//               keeps one row per TMEM lane (M = N = 128 per sub-tile) for
-//               its per-row head sums.  Two 256-column accumulators, so a
-//               pair's epilogue overlaps the next pair
+//               operands -> fp32 in TMEM.  Every layer runs transposed:
+//               M = 128 output channels (A = the weight tile), N = 256 rows
+//               of the pair (B = the window from row 16 + shift; any row:
+//               the swizzle phase follows the address), so TMEM lane =
+//               channel and column = row, and a pair takes half the MMA
+//               instructions of two M = N = 128 products (the issue rate of
+//               those bounded the kernel).  Two 256-column accumulators, so
+//               a pair's epilogue overlaps the next pair
 //   warps 2-9   epilogue, two warps per TMEM lane quadrant: fused bias /
 //               folded BatchNorm / ReLU / residual / next block's BN-ReLU,
-//               bf16 into 128B-swizzled shared memory, TMA store.
-//               Transposed layers read TMEM with tcgen05.ld 16x256b (the
-//               mma fragment layout) and transpose 8x8 blocks into the
-//               row-major staging tile with stmatrix .trans; the residual
-//               comes back the same way through ldmatrix .trans, and is
-//               prefetched into L2 a pair ahead.  The last layer reads
-//               32x32b (one row per thread) and computes the heads' 1x1
-//               convolutions per row.
+//               bf16 into 128B-swizzled shared memory, TMA store.  They
+//               read TMEM with tcgen05.ld 16x256b (the mma fragment
+//               layout) and transpose 8x8 blocks into the row-major
+//               staging tile with stmatrix .trans; the residual comes back
+//               the same way through ldmatrix .trans, and is prefetched
+//               into L2 a pair ahead.  The last layer computes the heads'
+//               1x1 convolutions from the same fragments: per-thread sums
+//               over its channels, a lane butterfly, then the four lane
+//               quadrants' partials added in order through shared memory.
 //
 // Every mbarrier wait is bounded: on timeout the kernel raises an error
 // flag, stops issuing, drains its own copies and releases TMEM.
@@ -212,21 +211,6 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // 16 TMEM lanes x 8 columns in the mma fragment layout: thread t receives
 // lane t/4 columns 2(t%4), 2(t%4)+1 (r[0], r[1]) and lane t/4 + 8, same
 // columns (r[2], r[3]).  Asynchronous until tmem_wait_ld().
@@ -270,9 +254,9 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
-// instruction descriptor (idesc_for below): D f32 (bits 4-5), A/B format
+// instruction descriptor (idesc_tr below): D f32 (bits 4-5), A/B format
 // (bits 7-9 / 10-12: 0 f16, 1 bf16), K-major A and B, N >> 3 at bit 17,
-// M >> 4 at bit 24; here M = N = 128
+// M >> 4 at bit 24
 
 // byte offset of 16-byte chunk `chunk` of row `row` in a 128B-swizzled
 // [rows x 128 B] tile (TMA SWIZZLE_128B pattern)
@@ -307,14 +291,8 @@ struct F16Traits<__half> {
   }
 };
 
-template <typename T>
-__host__ __device__ constexpr uint32_t idesc_for() {
-  return (1u << 4) | (F16Traits<T>::kFormat << 7) | (F16Traits<T>::kFormat << 10) | ((128u >> 3) << 17) |
-         ((128u >> 4) << 24);
-}
-
-// the transposed product of the residual layers: M = 128 output channels
-// (A = a weight tile), N = 256 rows of a tile pair (B = the window)
+// the transposed product of every layer: M = 128 output channels (A = a
+// weight tile), N = 256 rows of a tile pair (B = the window)
 template <typename T>
 __host__ __device__ constexpr uint32_t idesc_tr() {
   return (1u << 4) | (F16Traits<T>::kFormat << 7) | (F16Traits<T>::kFormat << 10) | ((256u >> 3) << 17) |
@@ -357,114 +335,14 @@ struct SmemLayout {
   static constexpr int kOut0Off = kOut1Off + 2 * kTileBytes;           // 2 halves x 16 KB
   static constexpr int kParamOff = kOut0Off + 2 * kTileBytes;          // floats
   static constexpr int kParamFloats = 3 * kC + kHeadCh * kC + 8;
-  static constexpr int kHeadPartOff = kParamOff + kParamFloats * 4;  // [128 rows][kHeadCh] floats
-  static constexpr int kBarOff = kHeadPartOff + kBM * kHeadCh * 4;
+  static constexpr int kHeadPartOff = kParamOff + kParamFloats * 4;  // [4 quads][128 rows][kHeadCh] floats
+  static constexpr int kBarOff = kHeadPartOff + 4 * kBM * kHeadCh * 4;
   static constexpr int kNumBars = 2 + 2 + 2 * kMaxBStages + 2 + 2;
   static constexpr int kBytes = kBarOff + 8 * kNumBars + 16 + 1024;  // + alignment slack
 };
 static_assert(SmemLayout::kBOff % 1024 == 0 && SmemLayout::kOut1Off % 1024 == 0, "swizzled tiles 1024-aligned");
 static_assert(kBTileBytes == kTileBytes, "weight stages and staging halves share a size");
 static_assert(SmemLayout::kBytes <= 227 * 1024, "shared memory budget");
-
-// One 128-row accumulator of a tile: bias / folded BatchNorm / ReLU /
-// residual / next block's BN-ReLU, 16-bit outputs staged 128B-swizzled for
-// the TMA store, or the heads' 1x1 convolutions per row.  Each thread owns
-// one row of the tile (its warp's TMEM lane quadrant) and 64 of the 128
-// columns (`half`); the two warps of a quadrant split the columns.  `head`
-// returns the row's partial head sums over its columns.
-template <typename T, bool Split>
-__device__ __forceinline__ void epilogue_tile(const EpiParams &ep, const float *prm, uint32_t acc_addr, int tile,
-                                              int quad, int half, int lane, uint8_t *out0, uint8_t *out1,
-                                              float (&head)[kHeadCh]) {
-  const int row_in_tile = quad * 32 + lane;
-  const int r = tile * kBM + row_in_tile;
-  const int p = r % kRowsPerBoard;
-  const bool real = r < ep.rows_valid && p >= 10 && (p % 10) != 9;
-#pragma unroll
-  for (int h = 0; h < kHeadCh; ++h) head[h] = 0.0f;
-  for (int ch = 2 * half; ch < 2 * half + 2; ++ch) {
-    // the residual's global loads go out before the accumulator read waits
-    uint4 ru[4];
-    float4 rf[8];  // split operands: the fp32 residual stream
-    if (ep.mode != kEpiConv1) {
-      if (Split) {
-        const float4 *src = reinterpret_cast<const float4 *>(ep.x32 + (size_t)r * kC + ch * 32);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) rf[q] = real ? src[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      } else {
-        const uint4 *src =
-            reinterpret_cast<const uint4 *>(static_cast<const T *>(ep.residual) + (size_t)r * kC + ch * 32);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) ru[q] = real ? src[q] : make_uint4(0, 0, 0, 0);
-      }
-    }
-    float v[32];
-    tmem_ld32(acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)(ch * 32), v);
-    float res[32];
-    if (ep.mode != kEpiConv1) {
-      if (Split) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          res[4 * q] = rf[q].x;
-          res[4 * q + 1] = rf[q].y;
-          res[4 * q + 2] = rf[q].z;
-          res[4 * q + 3] = rf[q].w;
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const T *hb = reinterpret_cast<const T *>(&ru[q]);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) res[q * 8 + e] = F16Traits<T>::to_f(hb[e]);
-        }
-      }
-    }
-    uint32_t pk0[16], pk1[16];
-#pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      float o0[2], o1[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int n = ch * 32 + i + j;
-        float y = v[i + j] + prm[n];
-        if (ep.mode == kEpiConv1) {
-          y = real ? fmaxf(y, 0.0f) : 0.0f;
-          o0[j] = y;
-          o1[j] = 0.0f;
-        } else {
-          // residual stream stored in the 16-bit type like the reference's
-          // bf16 model, or fp32 with split operands (whose heads then read
-          // the fp32 activation)
-          const float xs = y + res[i + j];
-          const float xn = Split ? xs : F16Traits<T>::to_f(F16Traits<T>::from_f(xs));
-          const float a = fmaxf(fmaf(xn, prm[kC + n], prm[2 * kC + n]), 0.0f);
-          o0[j] = real ? xn : 0.0f;
-          o1[j] = real ? (Split ? a : F16Traits<T>::to_f(F16Traits<T>::from_f(a))) : 0.0f;
-          if (ep.mode == kEpiHeads) {
-#pragma unroll
-            for (int h = 0; h < kHeadCh; ++h) head[h] = fmaf(o1[j], prm[3 * kC + h * kC + n], head[h]);
-          }
-        }
-      }
-      pk0[i / 2] = F16Traits<T>::pack(o0[0], o0[1]);
-      pk1[i / 2] = F16Traits<T>::pack(o1[0], o1[1]);
-    }
-    if (ep.mode != kEpiHeads) {
-      // 32 channels = four 16-byte chunks of the 64-channel half `ch / 2`
-      uint8_t *h0 = out0 + (ch >> 1) * kTileBytes;
-      uint8_t *h1 = out1 + (ch >> 1) * kTileBytes;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int chunk = (ch & 1) * 4 + q;
-        *reinterpret_cast<uint4 *>(h0 + swz(row_in_tile, chunk)) =
-            make_uint4(pk0[4 * q], pk0[4 * q + 1], pk0[4 * q + 2], pk0[4 * q + 3]);
-        if (ep.mode == kEpiConv2)
-          *reinterpret_cast<uint4 *>(h1 + swz(row_in_tile, chunk)) =
-              make_uint4(pk1[4 * q], pk1[4 * q + 1], pk1[4 * q + 2], pk1[4 * q + 3]);
-      }
-    }
-  }
-}
 
 __device__ __forceinline__ bool row_real(const EpiParams &ep, int r) {
   const int p = r % kRowsPerBoard;
@@ -636,16 +514,132 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
   }
 }
 
-// heads: the row's two column halves' partial sums, bias, ReLU
-__device__ __forceinline__ void store_heads(const EpiParams &ep, const float *prm, int tile, int row_in_tile,
-                                            const float (&lo)[kHeadCh], const float *hi) {
+// The head layer (the last block's conv2) in the transposed layout: the
+// residual sum and the trunk's final BN + ReLU as in conv2, then the six 1x1
+// head channels per row.  Each thread sums its 4 channels' products for its
+// two rows of every 8-row block, the 8 lanes of a row pair add theirs with
+// an xor butterfly, and lanes 0-3 leave the warp's 32-channel partials in
+// `part` [quad][row][head]; store_heads_tr then adds the four quads in
+// order.  Without split operands the residual is 16-bit and staged through
+// out0 (as conv2); with them it is the fp32 stream, read element by element,
+// and the heads read the fp32 activation.
+template <typename T, bool Split>
+__device__ __forceinline__ void epilogue_tile_tr_heads(const EpiParams &ep, const float (&cst)[3][4],
+                                                       const float *prm, uint32_t acc_addr, int tile, int quad,
+                                                       int wh, int lane, uint8_t *out0, const uint4 (&res)[8],
+                                                       float *part) {
+  uint8_t *h0 = out0 + (quad >> 1) * kTileBytes;
+  const int row_base = wh * 64, chunk0 = (quad & 1) * 4;
+  if (!Split) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int idx = k * 32 + lane;
+      *reinterpret_cast<uint4 *>(h0 + swz(row_base + (idx >> 2), chunk0 + (idx & 3))) = res[k];
+    }
+    __syncwarp();
+  }
+  const int mrow = lane & 7, mat = lane >> 3;
+  const uint32_t lane_addr = acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)row_base;
+  const int ch0 = quad * 32 + lane / 4;  // + 8 m: this thread's channels
+  float hw[kHeadCh][4];
+#pragma unroll
+  for (int h = 0; h < kHeadCh; ++h)
+#pragma unroll
+    for (int m = 0; m < 4; ++m) hw[h][m] = prm[3 * kC + h * kC + ch0 + 8 * m];
+#pragma unroll 1
+  for (int jj = 0; jj < 4; ++jj) {
+    uint32_t d[2][2][4];
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2)
+#pragma unroll
+      for (int g = 0; g < 2; ++g) tmem_ld16x256(lane_addr + ((uint32_t)(16 * g) << 16) + 8 * (2 * jj + j2), d[j2][g]);
+    float rx[2][4][2];
+    if (Split) {
+#pragma unroll
+      for (int j2 = 0; j2 < 2; ++j2) {
+        const size_t r0 = (size_t)tile * kBM + row_base + 8 * (2 * jj + j2) + 2 * (lane & 3);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          rx[j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
+          rx[j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+        }
+      }
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int j2 = 0; j2 < 2; ++j2) {
+      const int rb = row_base + 8 * (2 * jj + j2);
+      const int r0 = tile * kBM + rb + 2 * (lane & 3);
+      const bool real0 = row_real(ep, r0), real1 = row_real(ep, r0 + 1);
+      if (!Split) {
+        uint32_t rv[4];
+        ldmatrix_x4_trans(smem_u32(h0 + swz(rb + mrow, chunk0 + mat)), rv);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const T *rh = reinterpret_cast<const T *>(&rv[m]);
+          rx[j2][m][0] = F16Traits<T>::to_f(rh[0]);
+          rx[j2][m][1] = F16Traits<T>::to_f(rh[1]);
+        }
+      }
+      float acc[kHeadCh][2];
+#pragma unroll
+      for (int h = 0; h < kHeadCh; ++h) acc[h][0] = acc[h][1] = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int g = m >> 1, hi = m & 1;
+        const float y0 = __uint_as_float(d[j2][g][2 * hi]) + cst[0][m];
+        const float y1 = __uint_as_float(d[j2][g][2 * hi + 1]) + cst[0][m];
+        float x0 = y0 + rx[j2][m][0], x1 = y1 + rx[j2][m][1];
+        if (!Split) {
+          // residual stream in the 16-bit type, heads on the 16-bit activation
+          x0 = F16Traits<T>::to_f(F16Traits<T>::from_f(x0));
+          x1 = F16Traits<T>::to_f(F16Traits<T>::from_f(x1));
+        }
+        float a0 = real0 ? fmaxf(fmaf(x0, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
+        float a1 = real1 ? fmaxf(fmaf(x1, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
+        if (!Split) {
+          a0 = F16Traits<T>::to_f(F16Traits<T>::from_f(a0));
+          a1 = F16Traits<T>::to_f(F16Traits<T>::from_f(a1));
+        }
+#pragma unroll
+        for (int h = 0; h < kHeadCh; ++h) {
+          acc[h][0] = fmaf(a0, hw[h][m], acc[h][0]);
+          acc[h][1] = fmaf(a1, hw[h][m], acc[h][1]);
+        }
+      }
+      // add the 8 lanes of this row pair (lane / 4 = channel within 8)
+#pragma unroll
+      for (int h = 0; h < kHeadCh; ++h)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int off = 4; off <= 16; off <<= 1) acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], off);
+      if (lane < 4) {
+        const int row = rb + 2 * lane;
+#pragma unroll
+        for (int h = 0; h < kHeadCh; ++h) {
+          part[(quad * kBM + row) * kHeadCh + h] = acc[h][0];
+          part[(quad * kBM + row + 1) * kHeadCh + h] = acc[h][1];
+        }
+      }
+    }
+  }
+}
+
+// heads: a row's four quad partials in order, bias, ReLU
+__device__ __forceinline__ void store_heads_tr(const EpiParams &ep, const float *prm, int tile, int row_in_tile,
+                                               const float *part) {
   const int r = tile * kBM + row_in_tile;
   if (r >= ep.rows_valid) return;
-  const int p = r % kRowsPerBoard;
-  const bool real = p >= 10 && (p % 10) != 9;
+  const bool real = row_real(ep, r);
   float hb[kHeadCh];
 #pragma unroll
-  for (int h = 0; h < kHeadCh; ++h) hb[h] = real ? fmaxf(lo[h] + hi[h] + prm[3 * kC + kHeadCh * kC + h], 0.0f) : 0.0f;
+  for (int h = 0; h < kHeadCh; ++h) {
+    float v = part[(0 * kBM + row_in_tile) * kHeadCh + h];
+#pragma unroll
+    for (int q = 1; q < 4; ++q) v += part[(q * kBM + row_in_tile) * kHeadCh + h];
+    hb[h] = real ? fmaxf(v + prm[3 * kC + kHeadCh * kC + h], 0.0f) : 0.0f;
+  }
   float4 *dst = reinterpret_cast<float4 *>(ep.head_out + (size_t)r * 8);
   dst[0] = make_float4(hb[0], hb[1], hb[2], hb[3]);
   dst[1] = make_float4(hb[4], hb[5], 0.0f, 0.0f);
@@ -677,14 +671,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
   uint64_t *b_empty = b_full + kMaxBStages;
   uint64_t *acc_full = b_empty + kMaxBStages;
   // weight stages: the staging tiles an epilogue mode leaves unused extend the ring
-  const int nbs = ep.mode == kEpiHeads ? kMaxBStages : (ep.mode == kEpiConv1 && !Split ? 6 : kBStages);
+  // (the head layer stages a 16-bit residual through out0; split operands
+  // read theirs from the fp32 stream and leave both staging tiles unused)
+  const int nbs = ep.mode == kEpiHeads ? (Split ? kMaxBStages : kBStages + 2)
+                                       : (ep.mode == kEpiConv1 && !Split ? 6 : kBStages);
   // windows per pair (hi and lo of each half with split operands) and the
   // weight tiles per (window, tap)
   const int nwin = Split ? 4 : 2;
   const int wlo_terms = Split && ep.terms == 3 ? 2 : 1;  // weight tiles per tap of a hi window
-  // the residual layers run transposed (TMEM lane = output channel, column =
-  // row, half the MMA instructions); the heads keep one row per TMEM lane
-  const bool tr = ep.mode != kEpiHeads;
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -816,25 +810,12 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
               tc_fence_after();
               const uint32_t sb = smem_u32(smem + SmemLayout::kBOff + bstage * kBTileBytes);
               const uint32_t acc = (wi | tap | term) != 0;
-              if (tr) {
-                // D[channel][row] of both sub-tiles: one N = 256 product per K step
-                const uint32_t wrow = win + (uint32_t)(kWinLead + off) * 128u;
+              // D[channel][row] of both sub-tiles: one N = 256 product per K step
+              const uint32_t wrow = win + (uint32_t)(kWinLead + off) * 128u;
 #pragma unroll
-                for (int k = 0; k < kBK / 16; ++k)
-                  umma_f16(d0, smem_desc_sw128(sb + k * 32), smem_desc_sw128(wrow + k * 32), idesc_tr<T>(),
-                           acc | (k != 0));
-              } else {
-#pragma unroll
-                for (int sub = 0; sub < 2; ++sub) {
-                  const int w = kWinLead + sub * kBM + off;  // window row of the sub-tile's row 0
-#pragma unroll
-                  for (int k = 0; k < kBK / 16; ++k) {
-                    const uint64_t adesc = smem_desc_sw128(win + (uint32_t)w * 128u + k * 32);
-                    const uint64_t bdesc = smem_desc_sw128(sb + k * 32);
-                    umma_f16(d0 + (uint32_t)(sub * kC), adesc, bdesc, idesc_for<T>(), acc | (k != 0));
-                  }
-                }
-              }
+              for (int k = 0; k < kBK / 16; ++k)
+                umma_f16(d0, smem_desc_sw128(sb + k * 32), smem_desc_sw128(wrow + k * 32), idesc_tr<T>(),
+                         acc | (k != 0));
               umma_commit(&b_empty[bstage]);
               if (++bstage == nbs) {
                 bstage = 0;
@@ -902,33 +883,24 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
         const int tile = pair * 2 + sub;
         if (tile >= num_tiles) break;  // uniform across the epilogue threads
         uint4 res[8];
-        if (!Split && tr && ep.mode == kEpiConv2) load_residual_tr<T>(ep, tile, quad, half, lane, res);
+        if (!Split && ep.mode != kEpiConv1) load_residual_tr<T>(ep, tile, quad, half, lane, res);
         if (ep.mode != kEpiHeads) {
           // the staging buffers are free once the previous store has read them
           if (et == 0) tma_store_wait_read();
           asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
         }
-        float head[kHeadCh];
-        if (tr && Split)
-          epilogue_tile_tr_split<T>(ep, cst, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane,
-                                    out0, out1);
-        else if (tr)
-          epilogue_tile_tr<T>(ep, cst, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane, out0,
-                              out1, res);
-        else
-          epilogue_tile<T, Split>(ep, prm, tmem_base + (uint32_t)((2 * slot + sub) * kC), tile, quad, half, lane,
-                                  out0, out1, head);
+        const uint32_t acc_addr = tmem_base + (uint32_t)((2 * slot + sub) * kC);
         if (ep.mode == kEpiHeads) {
-          const int row_in_tile = quad * 32 + lane;
-          if (half == 1) {
-#pragma unroll
-            for (int h = 0; h < kHeadCh; ++h) head_part[row_in_tile * kHeadCh + h] = head[h];
-          }
+          epilogue_tile_tr_heads<T, Split>(ep, cst, prm, acc_addr, tile, quad, half, lane, out0, res, head_part);
           asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
-          if (half == 0) store_heads(ep, prm, tile, row_in_tile, head, head_part + row_in_tile * kHeadCh);
-          asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");  // partials consumed
+          if (et < kBM) store_heads_tr(ep, prm, tile, et, head_part);
+          asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");  // partials and staging consumed
           continue;
         }
+        if (Split)
+          epilogue_tile_tr_split<T>(ep, cst, acc_addr, tile, quad, half, lane, out0, out1);
+        else
+          epilogue_tile_tr<T>(ep, cst, acc_addr, tile, quad, half, lane, out0, out1, res);
         fence_proxy_async();
         asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory");
         if (et == 0) {
