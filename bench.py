@@ -754,7 +754,8 @@ def run_reference(args, world: int, rank: int) -> None:
 
     population = (args.workload or ("population" if world > 1 else "full")) == "population"
     cores = os.cpu_count() or 1
-    chunks = [(i, i + 1, population) for i in range(cores)]
+    per_process = 2  # lanes per process and step
+    chunks = [(i * per_process, (i + 1) * per_process, population) for i in range(cores)]
     ctx = mp.get_context("spawn")
     with ctx.Pool(cores) as pool:
         for _ in range(args.warmup):
@@ -774,8 +775,8 @@ def run_reference(args, world: int, rank: int) -> None:
         "config": full_workload_config(1, population, "fp32 (CPU)"),
         "leaf_evals_per_s": round(done * (FULL_SIMS + 1) / dt, 2),
         "cpu_baseline": {"value": round(value, 2), "unit": "sims/s", "cores": cores, "kind": "port",
-                         "sample": f"{done} lanes of the {FULL_LANES}-lane workload per step, one lane per process, "
-                                   f"{cores} processes"},
+                         "sample": f"{done} lanes of the {FULL_LANES}-lane workload per step, {per_process} lanes per "
+                                   f"process, {cores} single-threaded processes"},
         "e2e": {"value": round(value, 2), "unit": "sims/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is pure JAX (jax/flax/pgx not installable offline); timed: the C search "
                 "restatement with the fp32 network and Hex restatements, all host cores",

@@ -20,7 +20,7 @@ TREE_FIELDS = ("parents", "children_index", "node_to_play", "node_categorical_ou
 
 
 def run_cuda(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, native=True, lanes=None,
-             **env):
+             max_depth=None, **env):
     from scacchi_b200 import dirichlet_mctx as dm
     from scacchi_b200 import random as R
     from scacchi_b200.synthetic import SyntheticGame, SyntheticGameConfig
@@ -32,18 +32,20 @@ def run_cuda(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1
     rec = game if native else (lambda p, k, a, e: game(p, k, a, e))
     stats = torch.zeros(6, dtype=torch.int64, device="cuda")
     out = dm.dirichlet_thompson_policy((), R.PRNGKey(key_seed), root=root, recurrent_fn=rec, num_simulations=N,
-                                       posterior_update=rule, max_depth=N, policy_samples=samples, stats=stats)
+                                       posterior_update=rule, max_depth=N if max_depth is None else max_depth,
+                                       policy_samples=samples, stats=stats)
     torch.cuda.synchronize()
     return out, stats.cpu().numpy()
 
 
-def run_oracle(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, lanes=None, **env):
+def run_oracle(B, N, prefix, terminal_prob, seed=0, key_seed=0, samples=8, kappa=1.0, lanes=None, max_depth=None,
+               **env):
     from oracle import oracle as O
 
     env = O.synth_params(seed=seed, terminal_prob=terminal_prob, **env)
     return O.search_synthetic(env, B, O.PRNGKey(key_seed), N, O.Rule(prefix_cdf=prefix, kappa=kappa,
                                                                       samples=samples),
-                              max_depth=N, policy_samples=samples, lanes=lanes)
+                              max_depth=N if max_depth is None else max_depth, policy_samples=samples, lanes=lanes)
 
 
 def compare(out, want, lanes=slice(None)):
@@ -84,6 +86,17 @@ def test_population_chunks_bit_exact(cuda, samples):
     # several sample chunks, the last one partial
     out, _ = run_cuda(16, 12, False, 0.05, seed=6, key_seed=7, samples=samples)
     want = run_oracle(16, 12, False, 0.05, seed=6, key_seed=7, samples=samples)
+    compare(out, want)
+
+
+@pytest.mark.parametrize("B,N,max_depth", [(1, 1, 1), (1, 8, 1), (33, 3, 2), (2, 5, 5), (33, 1, None)],
+                         ids=["one_lane_one_sim", "depth_one", "ragged_batch", "two_lanes", "one_sim"])
+@pytest.mark.parametrize("prefix", [True, False], ids=["prefix_cdf", "mc"])
+def test_edge_shapes_bit_exact(cuda, B, N, max_depth, prefix):
+    """Batches of one lane and a batch that is not a multiple of 32, a
+    single simulation, and a depth limit of one (search.py:192-197)."""
+    out, _ = run_cuda(B, N, prefix, 0.1, seed=11, key_seed=12, max_depth=max_depth)
+    want = run_oracle(B, N, prefix, 0.1, seed=11, key_seed=12, max_depth=max_depth)
     compare(out, want)
 
 
