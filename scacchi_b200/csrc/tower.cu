@@ -607,20 +607,36 @@ __device__ __forceinline__ void epilogue_tile_tr_heads(const EpiParams &ep, cons
           acc[h][1] = fmaf(a1, hw[h][m], acc[h][1]);
         }
       }
-      // add the 8 lanes of this row pair (lane / 4 = channel within 8)
+      // add the 8 lanes of this row pair (lane / 4 = channel within 8) by
+      // reduce-scatter: 16 slots (head h, row i at 2 h + i; 12-15 empty),
+      // each xor step keeps the half named by this lane's bit and adds the
+      // partner's copy of it, so lane q = lane / 4 ends with head q's two rows
+      float v[16];
 #pragma unroll
-      for (int h = 0; h < kHeadCh; ++h)
+      for (int h = 0; h < kHeadCh; ++h) {
+        v[2 * h] = acc[h][0];
+        v[2 * h + 1] = acc[h][1];
+      }
 #pragma unroll
-        for (int i = 0; i < 2; ++i)
+      for (int k = 2 * kHeadCh; k < 16; ++k) v[k] = 0.0f;
 #pragma unroll
-          for (int off = 4; off <= 16; off <<= 1) acc[h][i] += __shfl_xor_sync(0xffffffffu, acc[h][i], off);
-      if (lane < 4) {
-        const int row = rb + 2 * lane;
+      for (int step = 0, width = 8; step < 3; ++step, width >>= 1) {
+        const int off = 16 >> step;          // lane bits 4, 3, 2
+        const bool upper = (lane & off) != 0;
 #pragma unroll
-        for (int h = 0; h < kHeadCh; ++h) {
-          part[(quad * kBM + row) * kHeadCh + h] = acc[h][0];
-          part[(quad * kBM + row + 1) * kHeadCh + h] = acc[h][1];
+        for (int k = 0; k < 8; ++k) {
+          if (k < width) {
+            const float send = upper ? v[k] : v[width + k];
+            const float keep = upper ? v[width + k] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
         }
+      }
+      const int q = lane >> 2;
+      if (q < kHeadCh) {
+        const int row = rb + 2 * (lane & 3);
+        part[(quad * kBM + row) * kHeadCh + q] = v[0];
+        part[(quad * kBM + row + 1) * kHeadCh + q] = v[1];
       }
     }
   }
