@@ -957,52 +957,53 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
 // A CTA serves kStemBoards boards; each thread computes 8 adjacent
 // channels of one row (16 threads cover a row, so a warp stores two full
 // 256-byte rows per output).  For observations of {0, 1} planes (at most
-// 4) the CTA first tabulates, per tap, the weight sum of each of the 16
-// plane subsets, so a tap costs one table row instead of a product per
-// plane; other inputs take the direct products.
+// 4) a tap costs one row of a table of per-tap weight sums over the 16
+// plane subsets, instead of a product per plane; the table is built once
+// per forward by stem_table_kernel and read through the L1 cache.  Other
+// inputs take the direct products.
 // ---------------------------------------------------------------------------
 
 constexpr int kStemBoards = 8;
 constexpr int kStemThreads = 256;
 constexpr int kStemSubsets = 16;  // plane subsets of up to 4 planes
+constexpr size_t kStemTableBytes = (size_t)9 * kStemSubsets * kC * sizeof(float);
 
-size_t stem_smem_bytes(int in_planes) {
-  const int rows = 9 * (in_planes <= 4 ? kStemSubsets : in_planes);
-  return (size_t)rows * kC * sizeof(float) + kStemBoards * 128;
+size_t stem_smem_bytes(int) { return (size_t)kStemBoards * 128; }
+
+// The subset table [9 taps][16 subsets][128]: entry (tap, m) sums the
+// weights of the planes in m in increasing plane order.  A table row keeps
+// channel n = 8 g + 4 j + l at 64 j + 4 g + l, so the 16 threads of a stem
+// row read 256 contiguous bytes per float4 load.
+__global__ void __launch_bounds__(256) stem_table_kernel(int in_planes, const float *w, float *table) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 9 * kStemSubsets * kC; i += gridDim.x * blockDim.x) {
+    const int k = i % kC, m = (i / kC) % kStemSubsets, tap = i / (kStemSubsets * kC);
+    const int n = ((k & 63) >> 2) * 8 + (k >> 6) * 4 + (k & 3);
+    float v = 0.0f;
+    bool any = false;
+    for (int c = 0; c < in_planes; ++c)
+      if (m >> c & 1) {
+        const float wv = w[(tap * in_planes + c) * kC + n];
+        v = any ? v + wv : wv;
+        any = true;
+      }
+    table[i] = v;  // subsets naming planes >= in_planes are never looked up
+  }
 }
 
 // With split operands (Split) x is written in fp32 to x32 and a as the
 // pair a (hi) / a_lo of 16-bit matrices.
 template <typename T, bool Split>
-__global__ void __launch_bounds__(kStemThreads, 2) stem_kernel(const float *obs, int boards, int in_planes,
-                                                            const float *w, const float *b, const float *s1,
-                                                            const float *t1, T *x, T *a, float *x32, T *a_lo) {
+__global__ void __launch_bounds__(kStemThreads, 3) stem_kernel(const float *obs, int boards, int in_planes,
+                                                            const float *w, const float *sw, const float *b,
+                                                            const float *s1, const float *t1, T *x, T *a,
+                                                            float *x32, T *a_lo) {
   extern __shared__ float sm[];
   const bool table = in_planes <= 4;
-  // table: [9 taps][16 subsets][128]; otherwise the weights [9 * in_planes][128]
-  float *sw = sm;
-  uint8_t *masks = reinterpret_cast<uint8_t *>(sm + 9 * (table ? kStemSubsets : in_planes) * kC);  // [boards][11 * 11]
+  // sw: the subset table [9 taps][16 subsets][128] (table), else unused;
+  // w: the weights [9 * in_planes][128]
+  uint8_t *masks = reinterpret_cast<uint8_t *>(sm);  // [boards][11 * 11]
   const int e0 = blockIdx.x * kStemBoards;
   const int nb = min(kStemBoards, boards - e0);
-  if (table) {
-    // a table row keeps channel n = 8 g + 4 j + l at 64 j + 4 g + l, so the
-    // 16 threads of a row read 256 contiguous bytes per float4 load
-    for (int i = threadIdx.x; i < 9 * kStemSubsets * kC; i += kStemThreads) {
-      const int k = i % kC, m = (i / kC) % kStemSubsets, tap = i / (kStemSubsets * kC);
-      const int n = ((k & 63) >> 2) * 8 + (k >> 6) * 4 + (k & 3);
-      float v = 0.0f;
-      bool any = false;
-      for (int c = 0; c < in_planes; ++c)
-        if (m >> c & 1) {
-          const float wv = w[(tap * in_planes + c) * kC + n];
-          v = any ? v + wv : wv;
-          any = true;
-        }
-      sw[i] = v;  // subsets naming planes >= in_planes are never looked up
-    }
-  } else {
-    for (int i = threadIdx.x; i < 9 * in_planes * kC; i += kStemThreads) sw[i] = w[i];
-  }
   // plane-subset mask per cell on an 11 x 11 grid with a zero border
   int binary = table ? 1 : 0;
   if (table) {
@@ -1046,8 +1047,8 @@ __global__ void __launch_bounds__(kStemThreads, 2) stem_kernel(const float *obs,
           const int m = mb[(y + tap / 3) * 11 + (xx + tap % 3)];
           if (m == 0) continue;
           const float *lt = sw + (tap * kStemSubsets + m) * kC + 4 * g;
-          const float4 l0 = *reinterpret_cast<const float4 *>(lt);
-          const float4 l1 = *reinterpret_cast<const float4 *>(lt + 64);
+          const float4 l0 = __ldg(reinterpret_cast<const float4 *>(lt));
+          const float4 l1 = __ldg(reinterpret_cast<const float4 *>(lt + 64));
           acc[0] += l0.x;
           acc[1] += l0.y;
           acc[2] += l0.z;
@@ -1071,11 +1072,11 @@ __global__ void __launch_bounds__(kStemThreads, 2) stem_kernel(const float *obs,
               if (table) {
                 const float *wt = sw + (tap * kStemSubsets + (1 << c)) * kC + 4 * g;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = fmaf(ov, wt[(j >> 2) * 64 + (j & 3)], acc[j]);
+                for (int j = 0; j < 8; ++j) acc[j] = fmaf(ov, __ldg(wt + (j >> 2) * 64 + (j & 3)), acc[j]);
               } else {
-                const float *wt = sw + (tap * in_planes + c) * kC + n0;
+                const float *wt = w + (tap * in_planes + c) * kC + n0;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = fmaf(ov, wt[j], acc[j]);
+                for (int j = 0; j < 8; ++j) acc[j] = fmaf(ov, __ldg(wt + j), acc[j]);
               }
             }
           }
@@ -1379,9 +1380,10 @@ uint64_t scacchi_tower_rows(int32_t boards) {
 }
 
 size_t scacchi_tower_workspace_bytes(int32_t boards) {
-  // split operands: fp32 x + hi/lo of a and h; plain: three 16-bit matrices
+  // split operands: fp32 x + hi/lo of a and h; plain: three 16-bit matrices;
+  // then the head features and the stem's subset table
   const uint64_t rows = scacchi_tower_rows(boards);
-  return (size_t)rows * kC * (4 + 2 * 4) + (size_t)rows * 8 * 4;
+  return (size_t)rows * kC * (4 + 2 * 4) + (size_t)rows * 8 * 4 + kStemTableBytes;
 }
 
 int scacchi_conv3x3(const void *input, const void *weights, const float *bias, int32_t mode, int32_t boards,
@@ -1467,6 +1469,7 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
   uint16_t *h = split ? a_lo + rows * kC : a + rows * kC;
   uint16_t *h_lo = split ? h + rows * kC : nullptr;
   float *feat = reinterpret_cast<float *>((split ? h_lo : h) + rows * kC);
+  float *stem_table = feat + rows * 8;  // 16-byte aligned: rows is a multiple of 128
   // rows past the last board stay zero (they are padding for the last tile)
   const uint64_t used = (uint64_t)boards * kRowsPerBoard;
   if (rows > used) {
@@ -1480,18 +1483,14 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
   }
   const size_t smem = stem_smem_bytes(w->in_planes);
   const int stem_grid = (boards + kStemBoards - 1) / kStemBoards;
-  static std::atomic<size_t> stem_attr{0};
-  if (smem > 48 * 1024 && stem_attr.load() < smem) {
-    cudaFuncSetAttribute(stem_kernel<__half, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(stem_kernel<__nv_bfloat16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(stem_kernel<__half, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(stem_kernel<__nv_bfloat16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    stem_attr.store(smem);
+  if (w->in_planes <= 4) {
+    stem_table_kernel<<<(9 * kStemSubsets * kC + 255) / 256, 256, 0, st>>>(w->in_planes, w->stem_w, stem_table);
+    g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   }
 #define SCACCHI_STEM(TT, SPLIT)                                                                                     \
   stem_kernel<TT, SPLIT><<<stem_grid, kStemThreads, smem, st>>>(                                                   \
-      obs, boards, w->in_planes, w->stem_w, w->stem_b, w->bn_scale, w->bn_shift, reinterpret_cast<TT *>(x),        \
-      reinterpret_cast<TT *>(a), x32, reinterpret_cast<TT *>(a_lo))
+      obs, boards, w->in_planes, w->stem_w, stem_table, w->stem_b, w->bn_scale, w->bn_shift,                      \
+      reinterpret_cast<TT *>(x), reinterpret_cast<TT *>(a), x32, reinterpret_cast<TT *>(a_lo))
   if (w->fp16) {
     if (split) SCACCHI_STEM(__half, true);
     else SCACCHI_STEM(__half, false);
