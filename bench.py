@@ -86,7 +86,7 @@ CAPTURED = {
     "backward_warp_inst_per_step": dict(value=212923824 * 128, sources=SEARCH_SOURCES, sha="718be44c55403747"),
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
-    "conv_traffic_bytes_8192": dict(value=1296633451, sources=TOWER_SOURCES, sha="1f6ba39481e23680"),
+    "conv_traffic_bytes_8192": dict(value=1308919872, sources=TOWER_SOURCES, sha="c4f5f2b6d62b1d08"),
 }
 
 
