@@ -1152,38 +1152,69 @@ size_t head_smem_bytes(int A) {
   return (size_t)kHeadBoards * (kFeat + 3 * kC + 3 * A) * sizeof(float);
 }
 
-// sum over k < 128 of h[k] * w[k * stride]: lanes 32-wide butterflies per
-// 32-element block, blocks added in order
-__device__ __forceinline__ float warp_dot128(const float *h, const float *w, int stride, int lane) {
+// sum over k < 128 of h[k * hstride] * w[k * stride]: lanes 32-wide
+// butterflies per 32-element block, blocks added in order
+__device__ __forceinline__ float warp_dot128(const float *h, int hstride, const float *w, int stride, int lane) {
   float total = 0.0f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    float v = h[j * 32 + lane] * w[(j * 32 + lane) * stride];
+    float v = h[(j * 32 + lane) * hstride] * w[(j * 32 + lane) * stride];
     for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
     total = j == 0 ? v : total + v;
   }
   return total;
 }
 
+// acc[g] += x[k][g] * wv for the G = 16 boards of x's row k (boards
+// innermost, read as four broadcast float4s)
+__device__ __forceinline__ void fma_boards(float (&acc)[kHeadBoards], const float *xk, float wv) {
+  static_assert(kHeadBoards == 16, "four float4 per row");
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float4 v = *reinterpret_cast<const float4 *>(xk + 4 * q);
+    acc[4 * q] = fmaf(v.x, wv, acc[4 * q]);
+    acc[4 * q + 1] = fmaf(v.y, wv, acc[4 * q + 1]);
+    acc[4 * q + 2] = fmaf(v.z, wv, acc[4 * q + 2]);
+    acc[4 * q + 3] = fmaf(v.w, wv, acc[4 * q + 3]);
+  }
+}
+
+// Shared arrays keep the boards innermost ([k][G]), so one float4
+// broadcast feeds four boards' products; each output's sum over k keeps
+// its fixed order.
 __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards, HeadWeights hw, float *logits,
                                                    float *log_alpha_v, float *log_alpha_q, float *alpha_v,
                                                    float *alpha_q) {
   constexpr int G = kHeadBoards;
-  extern __shared__ float hs[];
+  extern __shared__ __align__(16) float hs[];
   const int A = hw.A, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  float *f = hs;                 // [G][81 * 6]
-  float *hv = f + G * kFeat;     // [G][128]
+  float *f = hs;                 // [81 * 6][G]
+  float *hv = f + G * kFeat;     // [128][G]
   float *hq = hv + G * kC;
   float *hc = hq + G * kC;
   float *mq = hc + G * kC;       // [G][2A]
   float *cq = mq + G * 2 * A;    // [G][A]
   const int e0 = blockIdx.x * G;
   const int nb = min(G, boards - e0);
-  for (int i = t; i < G * kFeat; i += 128) {
-    const int g = i / kFeat, k = i % kFeat;
-    const int pos = k / kHeadCh, c = k % kHeadCh;
+  // one (board, cell) per item, boards fastest: a cell's 8 head features
+  // are one 32-byte sector
+  for (int i = t; i < G * 81; i += 128) {
+    const int g = i % G, pos = i / G;
     const int y = pos / 9, x = pos % 9;
-    f[i] = g < nb ? feat[((size_t)(e0 + g) * kRowsPerBoard + (y + 1) * 10 + x) * 8 + c] : 0.0f;
+    float4 lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f), hi = lo;
+    if (g < nb) {
+      const float4 *src =
+          reinterpret_cast<const float4 *>(feat + ((size_t)(e0 + g) * kRowsPerBoard + (y + 1) * 10 + x) * 8);
+      lo = src[0];
+      hi = src[1];
+    }
+    float *dst = f + pos * kHeadCh * G + g;
+    dst[0 * G] = lo.x;
+    dst[1 * G] = lo.y;
+    dst[2 * G] = lo.z;
+    dst[3 * G] = lo.w;
+    dst[4 * G] = hi.x;
+    dst[5 * G] = hi.y;
   }
   __syncthreads();
   // policy logits: flatten (y, x, c) of the 2-channel policy features
@@ -1194,11 +1225,7 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
 #pragma unroll 4
     for (int pos = 0; pos < 81; ++pos)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const float wv = hw.policy_w[(pos * 2 + c) * A + a];
-#pragma unroll
-        for (int g = 0; g < G; ++g) acc[g] = fmaf(f[g * kFeat + pos * kHeadCh + c], wv, acc[g]);
-      }
+      for (int c = 0; c < 2; ++c) fma_boards(acc, f + (pos * kHeadCh + c) * G, hw.policy_w[(pos * 2 + c) * A + a]);
     for (int g = 0; g < nb; ++g) logits[(size_t)(e0 + g) * A + a] = acc[g];
   }
   // hidden layers (thread t = hidden unit t)
@@ -1210,33 +1237,30 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
       q[g] = hw.qdir_b1[t];
       c[g] = hw.qconc_b1[t];
     }
-#pragma unroll 4
+#pragma unroll 2
     for (int pos = 0; pos < 81; ++pos) {
       const float wv = hw.value_w1[pos * kC + t], wc = hw.qconc_w1[pos * kC + t];
       const float wq0 = hw.qdir_w1[(pos * 2) * kC + t], wq1 = hw.qdir_w1[(pos * 2 + 1) * kC + t];
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float *fp = f + g * kFeat + pos * kHeadCh;
-        v[g] = fmaf(fp[2], wv, v[g]);
-        c[g] = fmaf(fp[5], wc, c[g]);
-        q[g] = fmaf(fp[3], wq0, q[g]);
-        q[g] = fmaf(fp[4], wq1, q[g]);
-      }
+      const float *fp = f + pos * kHeadCh * G;
+      fma_boards(v, fp + 2 * G, wv);
+      fma_boards(c, fp + 5 * G, wc);
+      fma_boards(q, fp + 3 * G, wq0);
+      fma_boards(q, fp + 4 * G, wq1);
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      hv[g * kC + t] = fmaxf(v[g], 0.0f);
-      hq[g * kC + t] = fmaxf(q[g], 0.0f);
-      hc[g * kC + t] = fmaxf(c[g], 0.0f);
+      hv[t * G + g] = fmaxf(v[g], 0.0f);
+      hq[t * G + g] = fmaxf(q[g], 0.0f);
+      hc[t * G + g] = fmaxf(c[g], 0.0f);
     }
   }
   __syncthreads();
   // value head: 2 mean logits + 1 log-concentration, one warp per board
   for (int g = warp; g < nb; g += 4) {
-    const float *h = hv + g * kC;
-    const float m0 = warp_dot128(h, hw.value_mean_w, 2, lane) + hw.value_mean_b[0];
-    const float m1 = warp_dot128(h, hw.value_mean_w + 1, 2, lane) + hw.value_mean_b[1];
-    const float cv = warp_dot128(h, hw.value_conc_w, 1, lane) + hw.value_conc_b[0];
+    const float *h = hv + g;
+    const float m0 = warp_dot128(h, G, hw.value_mean_w, 2, lane) + hw.value_mean_b[0];
+    const float m1 = warp_dot128(h, G, hw.value_mean_w + 1, 2, lane) + hw.value_mean_b[1];
+    const float cv = warp_dot128(h, G, hw.value_conc_w, 1, lane) + hw.value_conc_b[0];
     if (lane == 0) {
       const int e = e0 + g;
       const float cc = fminf(fmaxf(cv, -80.0f), 80.0f);
@@ -1253,12 +1277,8 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
     float acc[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = hw.qdir_b2[j];
-#pragma unroll 8
-    for (int k = 0; k < kC; ++k) {
-      const float wv = hw.qdir_w2[k * 2 * A + j];
-#pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(hq[g * kC + k], wv, acc[g]);
-    }
+#pragma unroll 4
+    for (int k = 0; k < kC; ++k) fma_boards(acc, hq + k * G, hw.qdir_w2[k * 2 * A + j]);
 #pragma unroll
     for (int g = 0; g < G; ++g) mq[g * 2 * A + j] = acc[g];
   }
@@ -1266,12 +1286,8 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
     float acc[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = hw.qconc_b2[a];
-#pragma unroll 8
-    for (int k = 0; k < kC; ++k) {
-      const float wv = hw.qconc_w2[k * A + a];
-#pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(hc[g * kC + k], wv, acc[g]);
-    }
+#pragma unroll 4
+    for (int k = 0; k < kC; ++k) fma_boards(acc, hc + k * G, hw.qconc_w2[k * A + a]);
 #pragma unroll
     for (int g = 0; g < G; ++g) cq[g * A + a] = acc[g];
   }
