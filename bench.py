@@ -87,6 +87,11 @@ CAPTURED = {
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
     "conv_traffic_bytes_8192": dict(value=1308919872, sources=TOWER_SOURCES, sha="c4f5f2b6d62b1d08"),
+    # smsp__inst_executed.sum over every backward launch of one profile step
+    # of the full step (1024 lanes) / that step's backward node updates
+    # (profiles/backward_fullstep.md)
+    "backward_inst_per_node_prefix": dict(value=None, sources=SEARCH_SOURCES, sha=""),
+    "backward_inst_per_node_population": dict(value=None, sources=SEARCH_SOURCES, sha=""),
 }
 
 
@@ -246,7 +251,7 @@ def _barrier(world: int) -> None:
 
 
 def full_step_bench(steps: int, warmup: int, precision: str | None, population: bool, world: int, rank: int,
-                    local: int, e2e: bool = True, clocks: bool = True) -> dict:
+                    local: int, e2e: bool = True, clocks: bool = True, lanes: int = FULL_LANES) -> dict:
     """The full search step of ``full_workload_config`` on this rank's lanes,
     device-resident, then end to end from pinned host buffers."""
     import ctypes as C
@@ -266,8 +271,12 @@ def full_step_bench(steps: int, warmup: int, precision: str | None, population: 
     game = HexGame(9, device=dev)
     net = AZDirichletNet(init_params(0, he_all_layers=False), device=dev, precision=precision)
     cfg = population_config(FULL_SIMS) if population else prefix_cdf_config(FULL_SIMS)
-    search = make_search(game, make_evaluator(net), cfg)
-    state = game.random_roots(FULL_LANES, R.fold_in(R.PRNGKey(ROOT_SEED), rank), 0, 20)
+    # work counters of the search kernels (one atomic add per CTA): backward
+    # node updates [0], visited children gathered [1], Monte Carlo fallbacks
+    # [2]; descent nodes [4], priors gathered [5]
+    stats = torch.zeros(6, dtype=torch.int64, device=dev)
+    search = make_search(game, make_evaluator(net), cfg, stats=stats)
+    state = game.random_roots(lanes, R.fold_in(R.PRNGKey(ROOT_SEED), rank), 0, 20)
     key = sharding.device_key(R.PRNGKey(SEARCH_SEED))
     stream = torch.cuda.current_stream(dev)
     gather_ev = []  # per step: (step start, search done, gather done)
@@ -290,7 +299,8 @@ def full_step_bench(steps: int, warmup: int, precision: str | None, population: 
     torch.cuda.synchronize()
     gather_ev.clear()
     if steps == 0:
-        return {}
+        return {"work": [int(v) for v in stats.cpu().tolist()]}
+    stats.zero_()
     # live timing of the tower's convolutions and of the loop's phases
     _lib.check(_lib.lib().scacchi_tower_timing(steps * (FULL_SIMS + 1) + 4), "tower_timing")
     timer = S.PhaseTimer()
@@ -328,6 +338,7 @@ def full_step_bench(steps: int, warmup: int, precision: str | None, population: 
            "conv_ms_per_step": conv_ms.value / steps, "forwards": forwards.value,
            "conv_launch_ms": conv_ms.value / max(forwards.value, 1) / 12,
            "phases_ms_per_step": {k: v / steps for k, v in phases.items()}, "precision": net.precision,
+           "work_per_step": [v / steps for v in stats.cpu().tolist()],
            "terms": net.terms, "clocks": sampler.summary() if sampler else None}
     if not e2e:
         return out
@@ -364,6 +375,27 @@ def full_step_bench(steps: int, warmup: int, precision: str | None, population: 
     out["h2d_bytes"] = h2d
     out["d2h_bytes"] = d2h
     return out
+
+
+def backward_issue(f: dict, population: bool, sm_count: int) -> dict:
+    """Issue rate of the backward kernel inside the step: warp instructions
+    per node update (from an ncu capture of every backward launch of a
+    profile step, divided by that step's node updates) x node updates per
+    step (live counters) / live backward time, against 4 instructions per
+    SM per cycle at the sampled clock."""
+    name = "backward_inst_per_node_population" if population else "backward_inst_per_node_prefix"
+    per_node, prov = captured(name)
+    ms = f["phases_ms_per_step"]["backward"]
+    nodes = f["work_per_step"][0]
+    mhz = (f["clocks"] or {}).get("sm_mhz") or 1965.0
+    peak = sm_count * 4 * mhz / 1e3
+    achieved = per_node * nodes / (ms / 1e3) / 1e9 if per_node and ms > 0 else None
+    return {"bound": "issue", "kernel": "backward_cta_kernel", "achieved": None if achieved is None else round(achieved, 1),
+            "peak": round(peak, 1), "unit": "G warp-inst/s",
+            "frac": None if achieved is None else round(achieved / peak, 4),
+            "node_updates_per_step": int(nodes), "mc_fallbacks_per_step": int(f["work_per_step"][2]),
+            "inst_per_node": per_node, "inst_provenance": prov,
+            "peak_source": "4 schedulers x SMs x sampled SM clock"}
 
 
 def tower_roofline(f: dict, peaks: dict) -> dict:
@@ -804,6 +836,8 @@ def main() -> None:
     ap.add_argument("--no-sub", action="store_true", help="skip the sub-object workloads of the default line")
     ap.add_argument("--boards", type=int, default=TOWER_BOARDS,
                     help="tower --profile: boards per forward (smaller cases for ncu captures)")
+    ap.add_argument("--lanes", type=int, default=FULL_LANES,
+                    help="full / population --profile: lanes per GPU (smaller cases for ncu captures)")
     ap.add_argument("--profile", action="store_true",
                     help="profiling mode: warmup steps + one device-resident step, no JSON line "
                          "(for ncu captures of the bench workloads)")
@@ -862,8 +896,10 @@ def main() -> None:
             return
         population = workload == "population"
         if args.profile:
-            full_step_bench(0, args.warmup + 1, args.precision, population, world, rank, local, e2e=False,
-                            clocks=False)
+            w = full_step_bench(0, args.warmup + 1, args.precision, population, world, rank, local, e2e=False,
+                                clocks=False, lanes=args.lanes)["work"]
+            print(json.dumps({"profile_work": {"backward_nodes": w[0], "child_gathers": w[1], "mc_fallbacks": w[2],
+                                               "descent_nodes": w[4], "steps": args.warmup + 1}}), file=sys.stderr)
             return
         f = full_step_bench(args.steps, args.warmup, args.precision, population, world, rank, local)
         peaks = read_peaks()
@@ -885,9 +921,7 @@ def main() -> None:
             roof["step_share"] = {"tower_convs": round(f["conv_ms_per_step"] / ms, 4),
                                   **{k: round(v / ms, 4) for k, v in phases.items()},
                                   "gather": round(f["gather_ms"] / ms, 4)}
-            if "search_kernels" in sub:
-                roof["backward_issue"] = dict(sub["search_kernels"]["roofline"]["issue"],
-                                              workload="isolated search kernels (4096 x 128)")
+            roof["backward_issue"] = backward_issue(f, population, torch.cuda.get_device_properties(dev).multi_processor_count)
             line = {
                 "metric": METRIC, "value": round(lanes * FULL_SIMS / (ms / 1e3), 2), "unit": "sims/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
