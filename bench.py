@@ -90,8 +90,8 @@ CAPTURED = {
     # smsp__inst_executed.sum over every backward launch of one profile step
     # of the full step (1024 lanes) / that step's backward node updates
     # (profiles/backward_fullstep.md)
-    "backward_inst_per_node_prefix": dict(value=None, sources=SEARCH_SOURCES, sha=""),
-    "backward_inst_per_node_population": dict(value=None, sources=SEARCH_SOURCES, sha=""),
+    "backward_inst_per_node_prefix": dict(value=27874, sources=SEARCH_SOURCES, sha="718be44c55403747"),
+    "backward_inst_per_node_population": dict(value=156590, sources=SEARCH_SOURCES, sha="718be44c55403747"),
 }
 
 
