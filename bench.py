@@ -10,9 +10,10 @@ legal moves.  One step = one ``search(root_state, key)`` call through
 ``play_search.make_search``: root evaluation, 256 x (descent, Hex step,
 tower, expand, backward), root readout and target packing.
 
-Under torchrun (N > 1) the default is the lane-sharded population step:
-8192 lanes per GPU with the 64-sample Thompson-population estimator, the
-root targets all-gathered over NCCL at the end of the step (weak scaling).
+Under torchrun (any number of ranks) the default is the lane-sharded
+population step: 8192 lanes per GPU with the 64-sample Thompson-population
+estimator, the root targets all-gathered over NCCL at the end of the step
+(weak scaling).
 
 Other workloads (also sub-objects of the default line): ``search`` -- the
 isolated search kernels on 4096 lanes x 128 simulations with synthetic
@@ -219,6 +220,15 @@ def full_workload_config(world: int, population: bool, precision: str) -> dict:
 # ---------------------------------------------------------------------------
 # the full step (configs 4 and 5)
 # ---------------------------------------------------------------------------
+
+def default_workload() -> str:
+    """The full step (the metric's one-GPU configuration) when run as a
+    plain process; the population step (the lane-sharded multi-GPU
+    configuration) whenever torchrun launched the process, one rank
+    included, so a scaling series run under torchrun measures one
+    workload at every N."""
+    return "population" if "WORLD_SIZE" in os.environ else "full"
+
 
 def _max_over_ranks(x: float, world: int) -> float:
     if world == 1:
@@ -784,7 +794,7 @@ def run_reference(args, world: int, rank: int) -> None:
         return
     import multiprocessing as mp
 
-    population = (args.workload or ("population" if world > 1 else "full")) == "population"
+    population = (args.workload or default_workload()) == "population"
     cores = os.cpu_count() or 1
     per_process = 2  # lanes per process and step
     chunks = [(i * per_process, (i + 1) * per_process, population) for i in range(cores)]
@@ -848,7 +858,7 @@ def main() -> None:
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
-    workload = args.workload or ("population" if world > 1 else "full")
+    workload = args.workload or default_workload()
 
     import datetime
 
