@@ -87,7 +87,7 @@ CAPTURED = {
     "backward_warp_inst_per_step": dict(value=212923824 * 128, sources=SEARCH_SOURCES, sha="718be44c55403747"),
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
-    "conv_traffic_bytes_8192": dict(value=1308919872, sources=TOWER_SOURCES, sha="c4f5f2b6d62b1d08"),
+    "conv_traffic_bytes_8192": dict(value=1305994027, sources=TOWER_SOURCES, sha="9f477837e53b7ec1"),
     # smsp__inst_executed.sum over every backward launch of one profile step
     # of the full step (1024 lanes) / that step's backward node updates
     # (profiles/backward_fullstep.md)
