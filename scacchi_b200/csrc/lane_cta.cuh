@@ -20,17 +20,17 @@
 template <int W>
 struct Cta {
   static constexpr int kT = 32 * W;
-  float *red;        // [4][kT] reduction inputs
+  float *red;        // [2][kT] reduction inputs
   float *bc;         // [16] broadcast results
   float *pv;         // [W] per-warp argmax values
   int *pi;           // [W] per-warp argmax indices
   float *lx, *l1mx, *lj, *flp, *joint, *score;  // [Q]
   float *zc;         // [Q] zero counts (exact small integers)
-  float *D, *F, *X;   // [Qs][kT]; the Monte Carlo population reuses them for [kKeyChunk][kT] utilities
+  float *D, *F;       // [Qs][kT]; the Monte Carlo population reuses them for [kKeyChunk][kT] utilities
   uint8_t *Z;         // [Qs][kT] zero-CDF flags
   DrawKeys *keys;     // [kKeyChunk] derived keys of a chunk of samples
   int *best;          // [kKeyChunk] argmax of each sample of a chunk
-  float4 *shape;      // [2][kT] Gamma constants of the compacted sampled actions
+  float4 *shape;      // [2][kT] Gamma constants of the compacted sampled actions (shares Z's storage)
   int *live;          // [kT] compacted list of the actions that carry work
   float *ascale, *asafe;  // [kT] per-action density shift and normaliser
   float *zint, *jinc;     // [Q] integrand of a non-unresolved action; joint increments
@@ -39,15 +39,26 @@ struct Cta {
 
 constexpr int kKeyChunk = 16;
 
-// matrix rows: enough for Q grid points and, over D, F and X together, for
-// a chunk of sample utilities, their second variates and the redraw list
-__host__ __device__ constexpr int cta_rows(int Q) { return Q > kKeyChunk ? Q : kKeyChunk; }
+// matrix rows: enough for Q grid points and, over D and F together, for a
+// chunk of sample utilities (kKeyChunk rows), their second variates
+// (kKeyChunk rows) and the redraw list (kKeyChunk rows of 16-bit pairs)
+__host__ __device__ constexpr int cta_rows(int Q) { return Q > 3 * kKeyChunk / 2 ? Q : 3 * kKeyChunk / 2; }
+
+// The Monte Carlo draw's Gamma constants (8 kT floats) and the quadrature's
+// zero-CDF flags (rows x kT bytes) are never live in the same pass of a node
+// update, so they share one region.
+template <int W>
+__host__ __device__ constexpr size_t cta_shared_region_floats(int Q) {
+  return (size_t)8 * Cta<W>::kT > ((size_t)cta_rows(Q) * Cta<W>::kT + 3) / 4
+             ? (size_t)8 * Cta<W>::kT
+             : ((size_t)cta_rows(Q) * Cta<W>::kT + 3) / 4;
+}
 
 template <int W>
 __host__ __device__ constexpr size_t cta_smem_floats(int Q) {
-  return (size_t)8 * Cta<W>::kT + (size_t)4 * Cta<W>::kT + 16 + 2 * W + kKeyChunk +
+  return cta_shared_region_floats<W>(Q) + (size_t)2 * Cta<W>::kT + 16 + 2 * W + kKeyChunk +
          (size_t)kKeyChunk * (sizeof(DrawKeys) / sizeof(float)) + 3 * (size_t)Cta<W>::kT + 9 * (size_t)Q +
-         3 * (size_t)cta_rows(Q) * Cta<W>::kT + ((size_t)cta_rows(Q) * Cta<W>::kT + 3) / 4;
+         2 * (size_t)cta_rows(Q) * Cta<W>::kT;
 }
 
 template <int W>
@@ -56,9 +67,10 @@ __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
   Cta<W> c;
   float *p = smem;
   c.shape = reinterpret_cast<float4 *>(p);  // first: 16-byte aligned
-  p += 8 * Cta<W>::kT;
+  c.Z = reinterpret_cast<uint8_t *>(p);
+  p += cta_shared_region_floats<W>(Q);
   c.red = p;
-  p += 4 * Cta<W>::kT;
+  p += 2 * Cta<W>::kT;
   c.bc = p;
   p += 16;
   c.pv = p;
@@ -86,8 +98,6 @@ __device__ __forceinline__ Cta<W> cta_scratch(int Q) {
   const size_t m = (size_t)cta_rows(Q) * Cta<W>::kT;
   c.D = p;
   c.F = p + m;
-  c.X = p + 2 * m;
-  c.Z = reinterpret_cast<uint8_t *>(p + 3 * m);
   c.Q = Q;
   return c;
 }
@@ -107,6 +117,47 @@ __device__ __forceinline__ float column_sum(const float *col, int A, int lane) {
   }
   return butterfly_sum(p);
 }
+
+// canonical sum over actions of the clipped log-CDF of column `col`:
+// -inf where the CDF is zero (z set), else min(log CDF, 0)
+template <int W>
+__device__ __forceinline__ float column_sum_clipped(const float *f, const uint8_t *z, int A, int lane) {
+  float p = 0.0f;
+  bool first = true;
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    const int a = lane + kWarp * j;
+    if (a < A) {
+      const float fv = f[a];
+      const float x = z[a] ? -SM_INF : (fv < 0.0f ? fv : 0.0f);
+      p = first ? x : p + x;
+      first = false;
+    }
+  }
+  return butterfly_sum(p);
+}
+
+// The cells t, t + T, t + 2T, ... of a grid with n cells per row, as
+// (row, column) pairs: two divisions per walk instead of one per cell.
+// With n = 0 the grid is empty and the walk starts past every row.
+struct CellWalk {
+  int row, col, drow, dcol;
+  __device__ __forceinline__ CellWalk(int t, int T, int n) {
+    const int m = n > 0 ? n : 1;
+    row = n > 0 ? t / m : INT_MAX;
+    col = t - (n > 0 ? row : 0) * m;
+    drow = T / m;
+    dcol = T - drow * m;
+  }
+  __device__ __forceinline__ void next(int n) {
+    col += dcol;
+    row += drow;
+    if (col >= n) {
+      col -= n;
+      row += 1;
+    }
+  }
+};
 
 // Up to 4 simultaneous canonical sums over actions; every thread gets them.
 template <int W, int K>
@@ -139,7 +190,7 @@ __device__ __forceinline__ int cta_argmax_by_action(const Cta<W> &c, float v, in
   const int t = threadIdx.x, lane = t % kWarp, warp = t / kWarp;
   const float vv = t < A ? v : -SM_INF;
   const int ii = t < A ? t : INT_MAX;
-  c.red[3 * Cta<W>::kT + t] = vv;
+  c.red[Cta<W>::kT + t] = vv;
   const int wi = warp_argmax(vv, ii);
   if (lane == 0) c.pi[warp] = wi;
   __syncthreads();
@@ -148,7 +199,7 @@ __device__ __forceinline__ int cta_argmax_by_action(const Cta<W> &c, float v, in
 #pragma unroll
   for (int w = 0; w < W; ++w) {
     const int i = c.pi[w];
-    const float val = i == INT_MAX ? -SM_INF : c.red[3 * Cta<W>::kT + i];
+    const float val = i == INT_MAX ? -SM_INF : c.red[Cta<W>::kT + i];
     if (beats(val, i, bv, bi)) {
       bv = val;
       bi = i;
@@ -383,8 +434,8 @@ __device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, i
   const int a = threadIdx.x;
   float *const L[2] = {c.D, c.D + kKeyChunk * T};  // [kKeyChunk][T] each; L[0] becomes U
   uint16_t *redo = reinterpret_cast<uint16_t *>(c.D + 2 * kKeyChunk * T);  // 2 * kKeyChunk * T entries
-  for (int i = a; i < n * ns; i += T) {
-    const int s = i / ns, slot = i - s * ns;
+  for (CellWalk w(a, T, ns); w.row < n; w.next(ns)) {
+    const int s = w.row, slot = w.col;
     const int aa = c.live[slot];
     const uint64_t base = lane_base + (uint64_t)aa * 2u;
 #pragma unroll GU
@@ -407,15 +458,15 @@ __device__ void cta_draw_chunk(const Cta<W> &c, int n, int ns, const int *aug, i
     L[g][s * T + aa] = log_gamma_core(c.keys[s], lane_base + (uint64_t)aa * 2u + g, stride, gs);
   }
   __syncthreads();
-  for (int i = a; i < n * na; i += T) {
-    const int s = i / na, code = aug[i - s * na], slot = code >> 1, g = code & 1;
+  for (CellWalk w(a, T, na); w.row < n; w.next(na)) {
+    const int s = w.row, code = aug[w.col], slot = code >> 1, g = code & 1;
     const int aa = c.live[slot];
     float &lg = L[g][s * T + aa];
     lg = gamma_augment(c.keys[s], lane_base + (uint64_t)aa * 2u + g, c.shape[2 * slot + g].x, lg);
   }
   __syncthreads();
-  for (int i = a; i < n * ns; i += T) {
-    const int s = i / ns, aa = c.live[i - s * ns];
+  for (CellWalk w(a, T, ns); w.row < n; w.next(ns)) {
+    const int s = w.row, aa = c.live[w.col];
     L[0][s * T + aa] = binary_utility(L[0][s * T + aa], L[1][s * T + aa]);
   }
 }
@@ -541,7 +592,6 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &
   }
   __syncthreads();
   const float hstep = 0.5f * (hr / fh);
-  const int cells = n_unres * Q;
   // log-density of this action on the grid; a resolved or illegal action
   // has density 0 everywhere (so zero CDF and no log-CDF contribution)
   bool nan = false;
@@ -561,13 +611,12 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &
     for (int k = 0; k < Q; ++k) {
       c.D[k * T + a] = 0.0f;
       c.F[k * T + a] = 0.0f;
-      c.X[k * T + a] = 0.0f;
       c.Z[k * T + a] = 0;
     }
   }
   __syncthreads();
-  for (int i = a; i < cells; i += T) {
-    const int k = i / n_unres, aa = c.live[i - k * n_unres];
+  for (CellWalk w(a, T, n_unres); w.row < Q; w.next(n_unres)) {
+    const int k = w.row, aa = c.live[w.col];
     c.D[k * T + aa] = sm_expf(c.D[k * T + aa] - c.ascale[aa]);
   }
   __syncthreads();
@@ -594,22 +643,20 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &
     r.unsafe = true;
     return r;
   }
-  // per grid point: CDF, its log and the zero-CDF flag
-  for (int i = a; i < cells; i += T) {
-    const int k = i / n_unres, aa = c.live[i - k * n_unres];
+  // per grid point: CDF, its log and the zero-CDF flag (the clipped log-CDF
+  // of the joint is formed from the two in the column sums)
+  for (CellWalk w(a, T, n_unres); w.row < Q; w.next(n_unres)) {
+    const int k = w.row, aa = c.live[w.col];
     const float cd = c.F[k * T + aa] / c.asafe[aa];
     const bool pos = cd > 0.0f;
-    const float f = pos ? sm_logf(cd) : 0.0f;
-    const float m = f < 0.0f ? f : 0.0f;
-    c.F[k * T + aa] = f;
-    c.X[k * T + aa] = pos ? m : -SM_INF;
+    c.F[k * T + aa] = pos ? sm_logf(cd) : 0.0f;
     c.Z[k * T + aa] = pos ? 0 : 1;
   }
   __syncthreads();
   // leave-one-out products and the joint maximum CDF
   for (int k = warp; k < Q; k += W) {
     const float flp = column_sum<W>(c.F + k * T, A, lane);
-    const float lsum = column_sum<W>(c.X + k * T, A, lane);
+    const float lsum = column_sum_clipped<W>(c.F + k * T, c.Z + k * T, A, lane);
     int zl = 0;
 #pragma unroll
     for (int j = 0; j < W; ++j) zl += lane + kWarp * j < A ? c.Z[k * T + lane + kWarp * j] : 0;
@@ -636,8 +683,8 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &
     const float olp = (int)c.zc[k] > 0 ? -SM_INF : c.flp[k] - 0.0f;
     c.zint[k] = (0.0f / 1.0f) * sm_expf(olp);
   }
-  for (int i = a; i < cells; i += T) {
-    const int k = i / n_unres, aa = c.live[i - k * n_unres];
+  for (CellWalk w(a, T, n_unres); w.row < Q; w.next(n_unres)) {
+    const int k = w.row, aa = c.live[w.col];
     const float d = c.D[k * T + aa];
     const int zf = c.Z[k * T + aa];
     const float f = c.F[k * T + aa];
@@ -645,12 +692,13 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &
     c.D[k * T + aa] = (d / c.asafe[aa]) * sm_expf(olp);
   }
   __syncthreads();
-  // interval contributions (trapezoid of the integrand), clamped at 0
+  // interval contributions (trapezoid of the integrand), clamped at 0; the
+  // log-CDF rows are no longer read, so F holds them
   for (int k = 1; k < Q; ++k) {
     const float i0 = unres ? c.D[(k - 1) * T + a] : c.zint[k - 1];
     const float i1 = unres ? c.D[k * T + a] : c.zint[k];
     const float cc = hstep * (i0 + i1);
-    c.X[(k - 1) * T + a] = cc > 0.0f ? cc : (cc != cc ? cc : 0.0f);
+    c.F[(k - 1) * T + a] = cc > 0.0f ? cc : (cc != cc ? cc : 0.0f);
   }
   for (int j = a; j < Q - 1; j += T) {
     const float jinc = c.joint[j + 1] - c.joint[j];
@@ -658,18 +706,17 @@ __device__ PrefixResult1 cta_prefix_guarded(const Cta<W> &c, const NodeSummary &
   }
   __syncthreads();
   for (int j = warp; j < Q - 1; j += W) {
-    const float sc = column_sum<W>(c.X + j * T, A, lane);
+    const float sc = column_sum<W>(c.F + j * T, A, lane);
     if (lane == 0) c.score[j] = sc;
   }
   __syncthreads();
   // allocate each interval's joint increment in proportion to the
   // contributions (uniformly over unresolved actions if they sum to 0)
   const float uden = (float)(n_unres > 1 ? n_unres : 1);
-  const int icells = n_unres * (Q - 1);
-  for (int i = a; i < icells; i += T) {
-    const int j = i / n_unres, aa = c.live[i - j * n_unres];
+  for (CellWalk w(a, T, n_unres); w.row < Q - 1; w.next(n_unres)) {
+    const int j = w.row, aa = c.live[w.col];
     const float sc = c.score[j];
-    const float wgt = sc > 0.0f ? c.X[j * T + aa] / sc : 1.0f / uden;
+    const float wgt = sc > 0.0f ? c.F[j * T + aa] / sc : 1.0f / uden;
     c.D[j * T + aa] = wgt * c.jinc[j];
   }
   __syncthreads();
@@ -775,21 +822,27 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
 }
 
 // backward (search.py:146-171) with the built-in rules, one CTA per lane.
-// Shared memory limits the 3-warp prefix-CDF instance to 6 CTAs per SM and
-// its register budget matches (no spills); the 4-warp instance keeps a
-// budget for 5, since tighter ones spill.
 // RULE is the update rule of the launch (0: Monte Carlo, 1: guarded
-// prefix-CDF); the Monte Carlo instance carries no quadrature code, so it
-// needs fewer registers and more lanes fit on an SM.
+// prefix-CDF).  With 2 matrices of [max(Q, 24)][96] floats and the shared
+// Gamma-constant / zero-flag region, a 3-warp CTA takes 24.7 KB of shared
+// memory at Q = 21 (24.0 KB for the Monte Carlo instance).  The register
+// budgets are measured choices, not occupancy maxima: under a budget for
+// 8 or 9 CTAs the prefix-CDF instance compiles to 10-16 % more
+// instructions and, with more warps at different points of its large
+// code, stalls more on instruction fetch, so it runs slower than under the
+// budget for 6 (80 registers, 8 CTAs resident).  The Monte Carlo instance
+// is fastest under the budget for 9.  The 4-warp instances keep budgets
+// for 5 and 8, since tighter ones spill.
 #ifndef SCACCHI_BWD_MIN_BLOCKS
 #define SCACCHI_BWD_MIN_BLOCKS 6
 #endif
 #ifndef SCACCHI_BWD_MC_MIN_BLOCKS
-#define SCACCHI_BWD_MC_MIN_BLOCKS 8
+#define SCACCHI_BWD_MC_MIN_BLOCKS 9
 #endif
 
 template <int W, int RULE>
-__global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_BLOCKS : 5) : SCACCHI_BWD_MC_MIN_BLOCKS)
+__global__ void __launch_bounds__(32 * W, RULE == 1 ? (W < 4 ? SCACCHI_BWD_MIN_BLOCKS : 5)
+                                                    : (W < 4 ? SCACCHI_BWD_MC_MIN_BLOCKS : 8))
     backward_cta_kernel(Tree T, const uint32_t *key, const int32_t *sim_parent, const int32_t *sim_action,
                         const uint8_t *sim_active, const float2 *step_value, const int32_t *step_tp, UpdateParams P,
                         unsigned long long *stats) {
