@@ -71,24 +71,17 @@ SM_FN int sm_isnan(float x) { return x != x; }
 SM_FN int sm_isfinite(float x) { return (sm_f2u(x) & 0x7f800000u) != 0x7f800000u; }
 
 SM_FN float sm_logf(float x) {
-  if (!(x > 0.0f)) {
-    if (x == 0.0f) return -SM_INF;
-    return SM_NAN;  /* negative or NaN */
-  }
-  if (x == SM_INF) return x;
-  uint32_t u = sm_f2u(x);
-  int e = 0;
-  if (u < 0x00800000u) {  /* subnormal: scale by 2^23 exactly */
-    x = x * 8388608.0f;
-    u = sm_f2u(x);
-    e = -23;
-  }
-  e += (int)(u >> 23) - 127;
+  /* Zero, negative, NaN and infinite arguments are selected at the end
+   * instead of returned early, so the common path has no divergent branch;
+   * positive finite arguments take exactly the operations below. */
+  const int sub = sm_f2u(x) < 0x00800000u; /* subnormal (or zero): scale by 2^23 exactly */
+  const float xs = sub ? x * 8388608.0f : x;
+  const uint32_t u = sm_f2u(xs);
+  int e = (int)((u >> 23) & 0xffu) - 127 - (sub ? 23 : 0);
   float m = sm_u2f((u & 0x007fffffu) | 0x3f800000u);
-  if (m > 1.41421356f) {
-    m = m * 0.5f;
-    e += 1;
-  }
+  const int big = m > 1.41421356f;
+  m = big ? m * 0.5f : m;
+  e += big;
   float f = m - 1.0f;
   float s = f / (2.0f + f);
   float z = s * s;
@@ -98,7 +91,9 @@ SM_FN float sm_logf(float x) {
   float r = z * t;
   float lm = f - s * (f - r);
   float fe = (float)e;
-  return fmaf(fe, SM_LN2_HI, fmaf(fe, SM_LN2_LO, lm));
+  float v = fmaf(fe, SM_LN2_HI, fmaf(fe, SM_LN2_LO, lm));
+  v = x == SM_INF ? x : v;
+  return x > 0.0f ? v : (x == 0.0f ? -SM_INF : SM_NAN);
 }
 
 SM_FN float sm_ldexp_pos(float p, int k) {
@@ -109,11 +104,13 @@ SM_FN float sm_ldexp_pos(float p, int k) {
 }
 
 SM_FN float sm_expf(float x) {
-  if (sm_isnan(x)) return x;
-  if (x > 88.7228394f) return SM_INF;
-  if (x < -103.972084f) return 0.0f;
-  float k = rintf(x * SM_INV_LN2);
-  float r = fmaf(-k, SM_LN2_HI, x);
+  /* The special cases are selected at the end instead of returned early, so
+   * the common path has no divergent branch; in-range arguments take exactly
+   * the operations below. */
+  float xc = x > -103.972084f ? x : -103.972084f;
+  xc = xc < 88.7228394f ? xc : 88.7228394f;
+  float k = rintf(xc * SM_INV_LN2);
+  float r = fmaf(-k, SM_LN2_HI, xc);
   r = fmaf(-k, SM_LN2_LO, r);
   float p = fmaf(r, 1.98412698e-04f, 1.38888889e-03f);  /* 1/7!, 1/6! */
   p = fmaf(r, p, 8.33333333e-03f);                       /* 1/5! */
@@ -122,7 +119,15 @@ SM_FN float sm_expf(float x) {
   p = fmaf(r, p, 0.5f);
   p = fmaf(r, p, 1.0f);
   p = fmaf(r, p, 1.0f);
-  return sm_ldexp_pos(p, (int)k);
+  /* p * 2^k with one rounding at most (k in [-150, 128]): above 127 as
+   * (p * 2^(k-1)) * 2, below -126 as (p * 2^(k+64)) * 2^-64 */
+  const int ki = (int)k;
+  const int kk = ki > 127 ? ki - 1 : (ki < -126 ? ki + 64 : ki);
+  const float post = ki > 127 ? 2.0f : (ki < -126 ? 5.42101086e-20f : 1.0f);
+  float v = (p * sm_u2f((uint32_t)(kk + 127) << 23)) * post;
+  v = x > 88.7228394f ? SM_INF : v;
+  v = x < -103.972084f ? 0.0f : v;
+  return sm_isnan(x) ? x : v;
 }
 
 SM_FN float sm_log1pf(float x) {
