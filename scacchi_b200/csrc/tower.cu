@@ -38,7 +38,8 @@
 //               layout) and transpose 8x8 blocks into the row-major
 //               staging tile with stmatrix .trans; the residual comes back
 //               the same way through ldmatrix .trans, and is prefetched
-//               into L2 a pair ahead.  The last layer computes the heads'
+//               into L2 once the CTA's previous pair is done.  The last
+//               layer computes the heads'
 //               1x1 convolutions from the same fragments: per-thread sums
 //               over its channels, a lane butterfly, then the four lane
 //               quadrants' partials added in order through shared memory.
@@ -869,7 +870,11 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       cst[2][m] = prm[2 * kC + ch];
     }
     // the residual of a pair is read by the epilogue only: prefetch it into
-    // L2 one pair ahead so its loads do not wait on HBM
+    // L2 when this CTA's previous pair is done, so its loads do not wait on
+    // HBM.  That is about one mainloop ahead; a whole pair period ahead,
+    // the streaming traffic evicted a third of the prefetched lines before
+    // the epilogue read them (conv2 read 1.20 GB per 8192-board launch
+    // instead of 0.86).
     const bool has_res = ep.mode != kEpiConv1;
     auto prefetch_residual = [&](int p) {
       for (int sub = 0; sub < 2; ++sub) {
@@ -885,7 +890,6 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
     };
     if (has_res && et == 0) prefetch_residual(blockIdx.x);
     for (int pair = blockIdx.x; pair < num_pairs; pair += gridDim.x) {
-      if (has_res && et == 0) prefetch_residual(pair + gridDim.x);
       // one thread waits (bounded) and broadcasts, so the epilogue threads agree
       if (et == 0) {
         const bool ok = !*abort_flag && mbar_wait(&acc_full[slot], acc_phase, abort_flag);
@@ -933,6 +937,7 @@ __global__ void __launch_bounds__(kThreads, 1) conv_tc_kernel(const __grid_const
       // both accumulators of the pair can be reused by the MMA warp
       tc_fence_before();
       mbar_arrive(&acc_empty[slot]);
+      if (has_res && et == 0) prefetch_residual(pair + gridDim.x);
       if (++slot == 2) {
         slot = 0;
         acc_phase ^= 1u;
