@@ -93,3 +93,30 @@ def test_random_roots_are_reproducible_and_in_range():
     assert len({b.moves for b in boards}) > 5
     again = H.random_root(9, key, 17, 0, 20)
     assert np.array_equal(again.record(), boards[17].record())
+
+
+def test_action_layout_follows_the_reference_coordinates():
+    """The reference names Hex action a by column letter a % size and row
+    number a // size + 1 (scripts/checkpoint_moves.py:39-45; its vectors in
+    tests/test_checkpoint_moves.py:9-21, size 5).  The restatement indexes
+    cells the same way: the stone of action a lands at observation[row,
+    column] of that coordinate."""
+    for a, coord in [(0, "A1"), (4, "E1"), (5, "A2"), (12, "C3"), (24, "E5")]:
+        column, row = ord(coord[0]) - ord("A"), int(coord[1:]) - 1
+        obs = H.HexBoard(5).step(a).observation()
+        # the stone belongs to the player who just moved: the opponent plane
+        # of the side to move
+        assert obs[row, column, 1] == 1.0 and obs[..., 1].sum() == 1.0 and obs[..., 0].sum() == 0.0
+
+
+def test_initial_and_step_masks_follow_the_reference_call_site():
+    """envs.py:112-131 wraps pgx.hex.Hex(size): size * size + 1 actions, the
+    last (swap) never legal before a terminal state (`.at[-1].set(False)`
+    on init and on every step); the empty cells are the legal moves."""
+    for size in (5, 9):
+        b = H.HexBoard(size)
+        m = b.legal()
+        assert m.shape == (size * size + 1,) and m[:-1].all() and not m[-1]
+        b = b.step(size + 1)
+        m = b.legal()
+        assert not m[-1] and not m[size + 1] and m[:-1].sum() == size * size - 1
