@@ -39,3 +39,22 @@ def test_backward_issue_arithmetic(monkeypatch):
     assert abs(r["achieved"] - 30000 * 20000 / 0.1 / 1e9) < 0.1
     assert abs(r["peak"] - 148 * 4 * 1800 / 1e3) < 0.1
     assert r["node_updates_per_step"] == 20000 and r["mc_fallbacks_per_step"] == 5
+
+
+def test_default_workload_follows_the_launcher(monkeypatch):
+    """A plain process times the metric's one-GPU workload (the full step);
+    any torchrun launch, one rank included, times the population step, so a
+    scaling series measures one workload at every N."""
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    assert bench.default_workload() == "full"
+    for world in ("1", "2", "8"):
+        monkeypatch.setenv("WORLD_SIZE", world)
+        assert bench.default_workload() == "population"
+
+
+def test_stamped_figures_match_the_current_sources():
+    """Every stamped ncu figure was captured on the kernel sources as they
+    are now (a kernel change without a new capture shows up here)."""
+    for name in bench.CAPTURED:
+        value, prov = bench.captured(name)
+        assert value is not None and not prov["stale"], (name, prov)
