@@ -628,8 +628,10 @@ def search_kernels_bench(steps: int, warmup: int, world: int, rank: int, local: 
 def tower_bench(steps: int, warmup: int, precision: str | None = None, boards: int = TOWER_BOARDS) -> dict:
     """Residual tower alone: {0,1} planes (density 0.4), He-normal weights on
     every layer (seed 0), the library's default precision unless named.
-    The whole forward, then each convolution mode timed alone (random
-    operands, the forward's launch shape); stem + heads = the rest."""
+    The whole forward, with its 12 convolutions timed inside it by the
+    library (the roofline); then each convolution mode timed alone (random
+    operands, the forward's launch shape) for the per-mode breakdown; stem +
+    heads = the forward minus its convolutions."""
     import ctypes as C
 
     import torch
@@ -646,12 +648,18 @@ def tower_bench(steps: int, warmup: int, precision: str | None = None, boards: i
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the library times the 12 conv launches inside each timed forward
+    _lib.check(_lib.lib().scacchi_tower_timing(steps), "tower_timing")
     e0.record(stream)
     for _ in range(steps):
         net(obs)
     e1.record(stream)
     torch.cuda.synchronize()
+    conv_ms, forwards = C.c_float(0), C.c_int32(0)
+    _lib.check(_lib.lib().scacchi_tower_timing_read(C.byref(conv_ms), C.byref(forwards)), "tower_timing_read")
+    _lib.check(_lib.lib().scacchi_tower_timing(0), "tower_timing")
     ms = e0.elapsed_time(e1) / steps
+    conv_in_forward = conv_ms.value / max(forwards.value, 1)
     rows = int(_lib.lib().scacchi_tower_rows(boards))
     dt = torch.float16 if net.fp16 else torch.bfloat16
     gen = torch.Generator(device="cuda").manual_seed(0)
@@ -690,7 +698,6 @@ def tower_bench(steps: int, warmup: int, precision: str | None = None, boards: i
         torch.cuda.synchronize()
         mode_ms[name] = e0.elapsed_time(e1) / 10
     assert _lib.tower_error() == 0
-    conv_total = 6 * mode_ms["conv1"] + 5 * mode_ms["conv2"] + mode_ms["heads_layer"]
     peak = peaks["bf16_tflops"] / net.terms
     # the sustained figure is the rate cuBLAS holds under the power cap; the
     # tower measured right after a long step runs in that regime
@@ -699,15 +706,17 @@ def tower_bench(steps: int, warmup: int, precision: str | None = None, boards: i
     per_mode = {k: {"ms": round(v, 4), "tflops": round(alg / (v / 1e3) / 1e12, 1),
                     "frac": round(alg / (v / 1e3) / 1e12 / peak, 4),
                     "frac_sustained": round(alg / (v / 1e3) / 1e12 / peak_sus, 4)} for k, v in mode_ms.items()}
-    per_mode["stem_and_heads"] = {"ms": round(max(ms - conv_total, 0.0), 4)}
-    conv_avg = conv_total / 12
+    # the convolutions as timed inside the forward; the rest of the forward
+    # is the stem, the head kernel and the launches between them
+    per_mode["stem_and_heads"] = {"ms": round(max(ms - conv_in_forward, 0.0), 4)}
+    conv_avg = conv_in_forward / 12
     return {
         "boards": boards, "precision": net.precision, "ms_per_forward": round(ms, 4),
         "evals_per_s": round(boards / (ms / 1e3), 1),
         "tflops": round(TOWER_FLOP_PER_BOARD * boards / (ms / 1e3) / 1e12, 2),
         "forward_frac": round(TOWER_FLOP_PER_BOARD * boards / (ms / 1e3) / 1e12 / peak, 4),
         "per_mode": per_mode,
-        "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel (12-layer average)",
+        "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel (12-layer average, timed inside the forward)",
                      "achieved": round(alg / (conv_avg / 1e3) / 1e12, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(alg / (conv_avg / 1e3) / 1e12 / peak, 4), "avg_launch_ms": round(conv_avg, 4),
                      "frac_sustained": round(alg / (conv_avg / 1e3) / 1e12 / peak_sus, 4),
