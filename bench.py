@@ -87,7 +87,7 @@ CAPTURED = {
     "backward_warp_inst_per_step": dict(value=204322290 * 128, sources=SEARCH_SOURCES, sha="27cd0186f1860092"),
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
-    "conv_traffic_bytes_8192": dict(value=1145702912, sources=TOWER_SOURCES, sha="7568a953e85024fc"),
+    "conv_traffic_bytes_8192": dict(value=1147497472, sources=TOWER_SOURCES, sha="910876de414861e1"),
     # smsp__inst_executed.sum over every backward launch of one profile step
     # of the full step (1024 lanes) / that step's backward node updates
     # (profiles/backward_fullstep.md)

@@ -1139,6 +1139,8 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_kernel(const float *obs,
 // ---------------------------------------------------------------------------
 
 constexpr int kHeadBoards = 16;
+constexpr int kHeadHalf = kHeadBoards / 2;  // boards per thread: two threads share an output
+constexpr int kHeadThreads = 256;
 constexpr int kFeat = 81 * kHeadCh;
 
 struct HeadWeights {
@@ -1153,8 +1155,12 @@ struct HeadWeights {
   const float *qconc_w2, *qconc_b2;          // [128][A], [A]
 };
 
+// the features' region, reused for the Q heads' outputs once the hidden
+// layers have read the features
+__host__ __device__ inline int head_shared_floats(int A) { return kFeat > 3 * A ? kFeat : 3 * A; }
+
 size_t head_smem_bytes(int A) {
-  return (size_t)kHeadBoards * (kFeat + 3 * kC + 3 * A) * sizeof(float);
+  return (size_t)kHeadBoards * (head_shared_floats(A) + 3 * kC) * sizeof(float);
 }
 
 // sum over k < 128 of h[k * hstride] * w[k * stride]: lanes 32-wide
@@ -1172,10 +1178,12 @@ __device__ __forceinline__ float warp_dot128(const float *h, int hstride, const 
 
 // acc[g] += x[k][g] * wv for the G = 16 boards of x's row k (boards
 // innermost, read as four broadcast float4s)
-__device__ __forceinline__ void fma_boards(float (&acc)[kHeadBoards], const float *xk, float wv) {
-  static_assert(kHeadBoards == 16, "four float4 per row");
+// acc[g] += xk[g] * wv for this thread's kHeadHalf boards (xk already
+// offset to them): two float4 broadcasts per k
+__device__ __forceinline__ void fma_boards(float (&acc)[kHeadHalf], const float *xk, float wv) {
+  static_assert(kHeadHalf == 8, "two float4 per row");
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < 2; ++q) {
     const float4 v = *reinterpret_cast<const float4 *>(xk + 4 * q);
     acc[4 * q] = fmaf(v.x, wv, acc[4 * q]);
     acc[4 * q + 1] = fmaf(v.y, wv, acc[4 * q + 1]);
@@ -1186,24 +1194,28 @@ __device__ __forceinline__ void fma_boards(float (&acc)[kHeadBoards], const floa
 
 // Shared arrays keep the boards innermost ([k][G]), so one float4
 // broadcast feeds four boards' products; each output's sum over k keeps
-// its fixed order.
-__global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards, HeadWeights hw, float *logits,
-                                                   float *log_alpha_v, float *log_alpha_q, float *alpha_v,
-                                                   float *alpha_q) {
-  constexpr int G = kHeadBoards;
+// its fixed order.  Two threads share an output, one per half of the
+// CTA's boards (thread t: output t % 128, boards 8 (t / 128) ...), so a
+// CTA runs 8 warps; the Q heads' outputs reuse the features' region, so
+// four CTAs fit on an SM.
+__global__ void __launch_bounds__(kHeadThreads, 4) head_kernel(const float *feat, int boards, HeadWeights hw,
+                                                               float *logits, float *log_alpha_v, float *log_alpha_q,
+                                                               float *alpha_v, float *alpha_q) {
+  constexpr int G = kHeadBoards, H = kHeadHalf;
   extern __shared__ __align__(16) float hs[];
   const int A = hw.A, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  float *f = hs;                 // [81 * 6][G]
-  float *hv = f + G * kFeat;     // [128][G]
+  float *f = hs;                                    // [81 * 6][G]
+  float *hv = f + G * head_shared_floats(A);        // [128][G]
   float *hq = hv + G * kC;
   float *hc = hq + G * kC;
-  float *mq = hc + G * kC;       // [G][2A]
-  float *cq = mq + G * 2 * A;    // [G][A]
+  float *mq = f;                                    // [G][2A], once the features are read
+  float *cq = mq + G * 2 * A;                       // [G][A]
   const int e0 = blockIdx.x * G;
   const int nb = min(G, boards - e0);
+  const int u = t & (kC - 1), g0 = (t >> 7) * H;    // this thread's output index and first board
   // one (board, cell) per item, boards fastest: a cell's 8 head features
   // are one 32-byte sector
-  for (int i = t; i < G * 81; i += 128) {
+  for (int i = t; i < G * 81; i += kHeadThreads) {
     const int g = i % G, pos = i / G;
     const int y = pos / 9, x = pos % 9;
     float4 lo = make_float4(0.0f, 0.0f, 0.0f, 0.0f), hi = lo;
@@ -1223,45 +1235,48 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
   }
   __syncthreads();
   // policy logits: flatten (y, x, c) of the 2-channel policy features
-  for (int a = t; a < A; a += 128) {
-    float acc[G];
+  for (int a = u; a < A; a += kC) {
+    float acc[H];
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = hw.policy_b[a];
+    for (int g = 0; g < H; ++g) acc[g] = hw.policy_b[a];
 #pragma unroll 4
     for (int pos = 0; pos < 81; ++pos)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) fma_boards(acc, f + (pos * kHeadCh + c) * G, hw.policy_w[(pos * 2 + c) * A + a]);
-    for (int g = 0; g < nb; ++g) logits[(size_t)(e0 + g) * A + a] = acc[g];
-  }
-  // hidden layers (thread t = hidden unit t)
-  {
-    float v[G], q[G], c[G];
+      for (int c = 0; c < 2; ++c)
+        fma_boards(acc, f + (pos * kHeadCh + c) * G + g0, hw.policy_w[(pos * 2 + c) * A + a]);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      v[g] = hw.value_b1[t];
-      q[g] = hw.qdir_b1[t];
-      c[g] = hw.qconc_b1[t];
+    for (int g = 0; g < H; ++g)
+      if (g0 + g < nb) logits[(size_t)(e0 + g0 + g) * A + a] = acc[g];
+  }
+  // hidden layers (hidden unit u)
+  {
+    float v[H], q[H], c[H];
+#pragma unroll
+    for (int g = 0; g < H; ++g) {
+      v[g] = hw.value_b1[u];
+      q[g] = hw.qdir_b1[u];
+      c[g] = hw.qconc_b1[u];
     }
 #pragma unroll 2
     for (int pos = 0; pos < 81; ++pos) {
-      const float wv = hw.value_w1[pos * kC + t], wc = hw.qconc_w1[pos * kC + t];
-      const float wq0 = hw.qdir_w1[(pos * 2) * kC + t], wq1 = hw.qdir_w1[(pos * 2 + 1) * kC + t];
-      const float *fp = f + pos * kHeadCh * G;
+      const float wv = hw.value_w1[pos * kC + u], wc = hw.qconc_w1[pos * kC + u];
+      const float wq0 = hw.qdir_w1[(pos * 2) * kC + u], wq1 = hw.qdir_w1[(pos * 2 + 1) * kC + u];
+      const float *fp = f + pos * kHeadCh * G + g0;
       fma_boards(v, fp + 2 * G, wv);
       fma_boards(c, fp + 5 * G, wc);
       fma_boards(q, fp + 3 * G, wq0);
       fma_boards(q, fp + 4 * G, wq1);
     }
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      hv[t * G + g] = fmaxf(v[g], 0.0f);
-      hq[t * G + g] = fmaxf(q[g], 0.0f);
-      hc[t * G + g] = fmaxf(c[g], 0.0f);
+    for (int g = 0; g < H; ++g) {
+      hv[u * G + g0 + g] = fmaxf(v[g], 0.0f);
+      hq[u * G + g0 + g] = fmaxf(q[g], 0.0f);
+      hc[u * G + g0 + g] = fmaxf(c[g], 0.0f);
     }
   }
-  __syncthreads();
+  __syncthreads();  // the features are read: mq and cq take their place
   // value head: 2 mean logits + 1 log-concentration, one warp per board
-  for (int g = warp; g < nb; g += 4) {
+  for (int g = warp; g < nb; g += kHeadThreads / 32) {
     const float *h = hv + g;
     const float m0 = warp_dot128(h, G, hw.value_mean_w, 2, lane) + hw.value_mean_b[0];
     const float m1 = warp_dot128(h, G, hw.value_mean_w + 1, 2, lane) + hw.value_mean_b[1];
@@ -1277,27 +1292,29 @@ __global__ void __launch_bounds__(128) head_kernel(const float *feat, int boards
       alpha_v[e * 2 + 1] = expf(cc + (m1 - lse));
     }
   }
-  // Q heads
-  for (int j = t; j < 2 * A; j += 128) {
-    float acc[G];
+  // Q heads: the 2A direction outputs, then the A concentration outputs
+  for (int j = u; j < 3 * A; j += kC) {
+    const bool dir = j < 2 * A;
+    const int jj = dir ? j : j - 2 * A;
+    const float *hk = dir ? hq : hc;
+    const float *wk = dir ? hw.qdir_w2 + jj : hw.qconc_w2 + jj;
+    const int wstride = dir ? 2 * A : A;
+    float acc[H];
+    const float bias = dir ? hw.qdir_b2[jj] : hw.qconc_b2[jj];
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = hw.qdir_b2[j];
+    for (int g = 0; g < H; ++g) acc[g] = bias;
 #pragma unroll 4
-    for (int k = 0; k < kC; ++k) fma_boards(acc, hq + k * G, hw.qdir_w2[k * 2 * A + j]);
+    for (int k = 0; k < kC; ++k) fma_boards(acc, hk + k * G + g0, wk[k * wstride]);
 #pragma unroll
-    for (int g = 0; g < G; ++g) mq[g * 2 * A + j] = acc[g];
-  }
-  for (int a = t; a < A; a += 128) {
-    float acc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = hw.qconc_b2[a];
-#pragma unroll 4
-    for (int k = 0; k < kC; ++k) fma_boards(acc, hc + k * G, hw.qconc_w2[k * A + a]);
-#pragma unroll
-    for (int g = 0; g < G; ++g) cq[g * A + a] = acc[g];
+    for (int g = 0; g < H; ++g) {
+      if (dir)
+        mq[(g0 + g) * 2 * A + jj] = acc[g];
+      else
+        cq[(g0 + g) * A + jj] = acc[g];
+    }
   }
   __syncthreads();
-  for (int i = t; i < nb * A; i += 128) {
+  for (int i = t; i < nb * A; i += kHeadThreads) {
     const int g = i / A, a = i % A;
     const float cc = fminf(fmaxf(cq[g * A + a], -80.0f), 80.0f);
     const float q0 = mq[g * 2 * A + 2 * a], q1 = mq[g * 2 * A + 2 * a + 1];
@@ -1573,8 +1590,8 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
     cudaFuncSetAttribute(head_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)head_smem);
     head_attr.store(head_smem);
   }
-  head_kernel<<<(boards + kHeadBoards - 1) / kHeadBoards, 128, head_smem, st>>>(feat, boards, hw, logits, log_alpha_v,
-                                                                                log_alpha_q, alpha_v, alpha_q);
+  head_kernel<<<(boards + kHeadBoards - 1) / kHeadBoards, kHeadThreads, head_smem, st>>>(
+      feat, boards, hw, logits, log_alpha_v, log_alpha_q, alpha_v, alpha_q);
   g_tower_launches.fetch_add(1, std::memory_order_relaxed);
   return cudaPeekAtLastError() == cudaSuccess ? SCACCHI_OK : SCACCHI_ECUDA;
 }
