@@ -80,19 +80,19 @@ CAPTURED = {
     # dram__bytes_read.sum + dram__bytes_write.sum of one backward launch
     # (simulation 64 of the isolated-search profile step;
     # profiles/backward_cta_search4096x128.md)
-    "backward_traffic_bytes": dict(value=23676416 + 1536, sources=SEARCH_SOURCES, sha="27cd0186f1860092"),
+    "backward_traffic_bytes": dict(value=23675648 + 1792, sources=SEARCH_SOURCES, sha="f8154eef933b56af"),
     # smsp__inst_executed.sum of that launch x 128 launches per step (an
     # all-launch capture of an earlier build gave 5 % less: the middle
     # simulation's paths are a little deeper than the step's average)
-    "backward_warp_inst_per_step": dict(value=204322290 * 128, sources=SEARCH_SOURCES, sha="27cd0186f1860092"),
+    "backward_warp_inst_per_step": dict(value=204322290 * 128, sources=SEARCH_SOURCES, sha="f8154eef933b56af"),
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
     "conv_traffic_bytes_8192": dict(value=1147497472, sources=TOWER_SOURCES, sha="910876de414861e1"),
     # smsp__inst_executed.sum over every backward launch of one profile step
     # of the full step (1024 lanes) / that step's backward node updates
     # (profiles/backward_fullstep.md)
-    "backward_inst_per_node_prefix": dict(value=26355, sources=SEARCH_SOURCES, sha="27cd0186f1860092"),
-    "backward_inst_per_node_population": dict(value=153300, sources=SEARCH_SOURCES, sha="27cd0186f1860092"),
+    "backward_inst_per_node_prefix": dict(value=26355, sources=SEARCH_SOURCES, sha="f8154eef933b56af"),
+    "backward_inst_per_node_population": dict(value=153300, sources=SEARCH_SOURCES, sha="f8154eef933b56af"),
 }
 
 

@@ -753,15 +753,30 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
   const bool present = a < A;
   const sk_key sim_key = {key[0], key[1]};
   sk_key k = sk_split(sim_key, (uint64_t)b);
-  auto searchable = [&](int n) {
-    bool s = false;
+  // A node's row -- its player, its categorical outcome and this thread's
+  // edge -- is loaded in one round, as soon as the node is known: the
+  // searchable test of a child and the next level's draw then share it,
+  // so a level waits for one round of dependent loads instead of two.
+  int row_tp = 0, row_child = -1, row_payload = 0;
+  int8_t row_outcome = kNoOutcome;
+  bool row_masked = true;
+  float2 row_alpha = make_float2(1.0f, 1.0f);
+  auto load_row = [&](int n) {
+    const size_t ni = T.node(b, n);
+    row_tp = T.to_play[ni];
+    row_outcome = T.node_outcome[ni];
     if (present) {
       const size_t e = T.edge(b, n, a);
-      s = !T.invalid[e] && T.edge_outcome[e] == kNoOutcome;
+      row_masked = T.invalid[e] || T.edge_outcome[e] != kNoOutcome;
+      row_child = T.children[e];
+      row_payload = T.edge_payload[e];
+      row_alpha = T.edge_alpha[e];
     }
-    return __syncthreads_or(s) != 0;
   };
-  const bool root_active = T.node_outcome[T.node(b, 0)] == kNoOutcome && searchable(0);
+  // any searchable edge: legal and not categorical
+  auto searchable = [&]() { return __syncthreads_or(present && !row_masked) != 0; };
+  load_row(0);
+  const bool root_active = row_outcome == kNoOutcome && searchable();
   int node = 0, next = 0, action = 0, depth = 0;
   bool cont = root_active;
   const uint64_t stride = (uint64_t)A * 2u;
@@ -771,21 +786,20 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
     visited_nodes += 1;
     const sk_key next_key = sk_split(k, 0), sel_key = sk_split(k, 1);
     node = next;
-    const int player = T.to_play[T.node(b, node)];
+    const int player = row_tp;
     bool masked = true;
     GammaShape g0 = gamma_shape(1.0f), g1 = g0;
     if (present) {
-      const size_t e = T.edge(b, node, a);
-      masked = T.invalid[e] || T.edge_outcome[e] != kNoOutcome;
+      masked = row_masked;
       if (!masked) {
-        const int child = T.children[e];
+        const int child = row_child;
         float2 alpha;
-        if (child != -1 && T.edge_payload[e] <= 0 && T.ok(child)) {
+        if (child != -1 && row_payload <= 0 && T.ok(child)) {
           const size_t ci = T.node(b, child);
           alpha = align2(T.value_prior[ci], T.to_play[ci], player);
           prior_gathers += 1;
         } else {
-          alpha = T.edge_alpha[e];
+          alpha = row_alpha;
         }
         g0 = gamma_shape(alpha.x);
         g1 = gamma_shape(alpha.y);
@@ -797,7 +811,8 @@ __global__ void __launch_bounds__(32 * W) simulate_cta_kernel(Tree T, const uint
     const bool visited = child != -1;
     const int safe = visited ? child : 0;
     depth += 1;
-    const bool selectable = T.node_outcome[T.node(b, safe)] == kNoOutcome && searchable(safe);
+    load_row(safe);  // the next level's row when the walk goes on
+    const bool selectable = row_outcome == kNoOutcome && searchable();
     cont = visited && selectable && depth < max_depth;
     next = child;
     k = next_key;
