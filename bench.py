@@ -21,8 +21,11 @@ network outputs; ``tower`` -- the residual tower alone on 16384 boards.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
        [--workload full|population|search|tower] [--precision NAME]
-Prints one JSON line on rank 0.  NCCL's communicator lines appear on
-stderr when NCCL_DEBUG=INFO is set in the environment.
+       [--no-cpu-baseline] [--no-sub] [--profile [--boards B] [--lanes L]]
+Prints one JSON line on rank 0 (the line that starts with '{').  With
+NCCL_DEBUG=INFO set, NCCL prints its communicator lines into the same
+output.  --profile runs warm-up steps and one device-resident step and
+prints no line, for ncu captures (--boards / --lanes: smaller cases).
 """
 
 from __future__ import annotations
