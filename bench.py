@@ -90,7 +90,7 @@ CAPTURED = {
     "backward_warp_inst_per_step": dict(value=204322290 * 128, sources=SEARCH_SOURCES, sha="f8154eef933b56af"),
     # dram bytes of the 12 conv launches of one 8192-board forward at the
     # default precision, averaged per launch (profiles/conv_tc_split_tower8192.md)
-    "conv_traffic_bytes_8192": dict(value=1147497472, sources=TOWER_SOURCES, sha="910876de414861e1"),
+    "conv_traffic_bytes_8192": dict(value=1146349397, sources=TOWER_SOURCES, sha="960603ed2aee9b4f"),
     # smsp__inst_executed.sum over every backward launch of one profile step
     # of the full step (1024 lanes) / that step's backward node updates
     # (profiles/backward_fullstep.md)
@@ -683,7 +683,7 @@ def tower_bench(steps: int, warmup: int, precision: str | None = None, boards: i
         sc, sf = t["bn_scale"][1], t["bn_shift"][1]
         if net.terms > 1:
             return L.scacchi_conv3x3_split(ptr(a_hi), ptr(a_lo), ptr(w), ptr(t["conv_b"][1]), mode, boards,
-                                           int(net.fp16), net.terms, ptr(sc), ptr(sf), ptr(x32), ptr(t["head_w"]),
+                                           int(net.fp16), net.terms, ptr(sc), ptr(sf), ptr(x32), 0, ptr(t["head_w"]),
                                            ptr(t["head_b"]), ptr(out0), ptr(out1), ptr(head), sh)
         return L.scacchi_conv3x3(ptr(a_hi), ptr(w), ptr(t["conv_b"][1]), mode, boards, int(net.fp16), ptr(sc),
                                  ptr(sf), ptr(res16), ptr(t["head_w"]), ptr(t["head_b"]), ptr(out0), ptr(out1),

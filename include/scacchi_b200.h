@@ -406,7 +406,12 @@ int scacchi_conv3x3(const void *input, const void *weights, const float *bias, i
 
 /* The same convolution on split operands (terms 2 or 3): the input is the
  * pair input (hi) + input_lo of 16-bit matrices, weights [terms == 3 ? 2 :
- * 1][9][128 out][128 in], and the residual stream x32 float32 [rows, 128].
+ * 1][9][128 out][128 in], and the residual stream x32 float32 [rows, 128],
+ * each row's channels permuted within their 32-channel block: channel
+ * 32 q + 8 m + l (l < 8, m < 4) is stored at 32 q + 4 l + m (so an epilogue
+ * thread's four channels of a row are one 16-byte vector).  With
+ * x32_natural_in = 1 the input x32 is read in the natural channel order
+ * (the stem's output, for the first block) and written back permuted.
  * mode 0: (out_hi, out_lo) = split(relu(conv + bias)); mode 1: x32 <- x' =
  * conv + bias + x32 (in place), (out_hi, out_lo) = split(relu(x' *
  * bn_scale + bn_shift)); mode 2: as mode 1 without the stores, then the six
@@ -414,8 +419,8 @@ int scacchi_conv3x3(const void *input, const void *weights, const float *bias, i
  * v rounded to 16 bits, lo = (v - hi) rounded to 16 bits. */
 int scacchi_conv3x3_split(const void *input, const void *input_lo, const void *weights, const float *bias,
                           int32_t mode, int32_t boards, int32_t fp16, int32_t terms, const float *bn_scale,
-                          const float *bn_shift, float *x32, const float *head_w, const float *head_b, void *out_hi,
-                          void *out_lo, float *head_out, void *stream);
+                          const float *bn_shift, float *x32, int32_t x32_natural_in, const float *head_w,
+                          const float *head_b, void *out_hi, void *out_lo, float *head_out, void *stream);
 
 /* Sticky tower error flags (bit 0: a bounded wait timed out); reading
  * synchronises and clears.  Launch counter of the tower kernels. */

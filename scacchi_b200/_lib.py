@@ -113,7 +113,7 @@ SIGNATURES = {
     "scacchi_tower_workspace_bytes": [I32],
     "scacchi_tower_forward": [C.POINTER(TowerWeights), P, I32, P, P, P, P, P, P, P],
     "scacchi_conv3x3": [P, P, P, I32, I32, I32, P, P, P, P, P, P, P, P, P],
-    "scacchi_conv3x3_split": [P, P, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P],
+    "scacchi_conv3x3_split": [P, P, P, P, I32, I32, I32, I32, P, P, P, I32, P, P, P, P, P, P],
     "scacchi_tower_error": [P],
     "scacchi_tower_launch_count": [],
     "scacchi_tower_timing": [I32],

@@ -306,6 +306,13 @@ __host__ __device__ constexpr uint32_t idesc_tr() {
 
 enum EpiMode : int { kEpiConv1 = 0, kEpiConv2 = 1, kEpiHeads = 2 };
 
+// The fp32 residual stream x32 keeps each row's channels permuted within
+// their 32-channel block: channel 32 q + 8 m + l (l < 8, m < 4) is stored
+// at 32 q + 4 l + m.  An epilogue thread holds channels 32 q + l + 8 m for
+// m < 4 (the mma fragment layout), so its four values of a row are one
+// 16-byte vector.
+__host__ __device__ constexpr int x32_slot(int c) { return (c & ~31) | ((c & 7) << 2) | ((c >> 3) & 3); }
+
 struct EpiParams {
   int mode;
   int rows_valid;            // E * 100; rows at or above are padding
@@ -314,7 +321,8 @@ struct EpiParams {
   const float *bn_scale;     // conv2: next block's BN1 (or the final BN), per channel
   const float *bn_shift;
   const void *residual;      // conv2 / heads: x of the block input, [rows, 128] 16-bit
-  float *x32;                // split operands: the fp32 residual stream [rows, 128], updated in place
+  float *x32;                // split operands: the fp32 residual stream [rows, 128] (channels in x32_slot order), updated in place
+  int x32_natural_in;        // x32 is read in the natural channel order (the stem's output) and written in x32_slot order
   const float *head_w;       // heads: [6][128] 1x1 conv weights (head BN folded)
   const float *head_b;       // [6]
   float *head_out;           // heads: [rows, 8] f32
@@ -435,9 +443,9 @@ __device__ __forceinline__ void epilogue_tile_tr(const EpiParams &ep, const floa
 // is written as a pair, hi = the value rounded to T into out0 and lo = the
 // remainder (exact in fp32) rounded to T into out1, so hi + lo carries about
 // twice T's significand into the next convolution; and the residual stream
-// x stays fp32 in ep.x32 (row-major [rows, 128], read and rewritten in place
-// element by element: for one (block, m) the warp covers 8 rows x 8
-// channels, whole 32-byte sectors).  conv1 writes h's pair; conv2 writes
+// x stays fp32 in ep.x32 ([rows, 128] with each row's channels in x32_slot
+// order, read and rewritten in place: a thread's four channels of a row are
+// one 16-byte vector).  conv1 writes h's pair; conv2 writes
 // x' = conv + bias + x to x32 and the pair of relu(bn(x')).
 template <typename T>
 __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, const float (&cst)[3][4],
@@ -450,6 +458,7 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
   const int mrow = lane & 7, mat = lane >> 3;
   const uint32_t lane_addr = acc_addr + ((uint32_t)(quad * 32) << 16) + (uint32_t)row_base;
   const int ch0 = quad * 32 + lane / 4;  // + 8 m: this thread's channels
+  const int xs = x32_slot(ch0);          // their four x32 slots, xs .. xs + 3
   // Software pipeline over the four 16-row steps jj: the accumulator
   // columns and the residual of step jj + 1 are requested before step jj
   // is computed, so their latency hides behind that step's arithmetic
@@ -466,10 +475,23 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
 #pragma unroll
       for (int j2 = 0; j2 < 2; ++j2) {
         const size_t r0 = (size_t)tile * kBM + row_base + 8 * (2 * jj + j2) + 2 * (lane & 3);
+        if (ep.x32_natural_in) {
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          rx[buf][j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
-          rx[buf][j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+          for (int m = 0; m < 4; ++m) {
+            rx[buf][j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
+            rx[buf][j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+          }
+        } else {
+          const float4 v0 = *reinterpret_cast<const float4 *>(ep.x32 + r0 * kC + xs);
+          const float4 v1 = *reinterpret_cast<const float4 *>(ep.x32 + (r0 + 1) * kC + xs);
+          rx[buf][j2][0][0] = v0.x;
+          rx[buf][j2][1][0] = v0.y;
+          rx[buf][j2][2][0] = v0.z;
+          rx[buf][j2][3][0] = v0.w;
+          rx[buf][j2][0][1] = v1.x;
+          rx[buf][j2][1][1] = v1.y;
+          rx[buf][j2][2][1] = v1.z;
+          rx[buf][j2][3][1] = v1.w;
         }
       }
     }
@@ -487,6 +509,7 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
       const bool real0 = row_real(ep, r0), real1 = row_real(ep, r0 + 1);
       const int srow = rb + mrow, schunk = chunk0 + mat;
       uint32_t p0[4], p1[4];
+      float xn[2][4];  // conv2: the updated residual of rows r0, r0 + 1
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const int g = m >> 1, hi = m & 1;
@@ -499,8 +522,8 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
         } else {
           const float x0 = real0 ? y0 + rx[cur][j2][m][0] : 0.0f;
           const float x1 = real1 ? y1 + rx[cur][j2][m][1] : 0.0f;
-          ep.x32[(size_t)r0 * kC + ch0 + 8 * m] = x0;
-          ep.x32[(size_t)(r0 + 1) * kC + ch0 + 8 * m] = x1;
+          xn[0][m] = x0;
+          xn[1][m] = x1;
           v0 = real0 ? fmaxf(fmaf(x0, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
           v1 = real1 ? fmaxf(fmaf(x1, cst[1][m], cst[2][m]), 0.0f) : 0.0f;
         }
@@ -508,6 +531,12 @@ __device__ __forceinline__ void epilogue_tile_tr_split(const EpiParams &ep, cons
         const float a1 = F16Traits<T>::to_f(F16Traits<T>::from_f(v1));
         p0[m] = F16Traits<T>::pack(a0, a1);
         p1[m] = F16Traits<T>::pack(v0 - a0, v1 - a1);
+      }
+      if (conv2) {
+        *reinterpret_cast<float4 *>(ep.x32 + (size_t)r0 * kC + xs) =
+            make_float4(xn[0][0], xn[0][1], xn[0][2], xn[0][3]);
+        *reinterpret_cast<float4 *>(ep.x32 + (size_t)(r0 + 1) * kC + xs) =
+            make_float4(xn[1][0], xn[1][1], xn[1][2], xn[1][3]);
       }
       stmatrix_x4_trans(smem_u32(h0 + swz(srow, schunk)), p0);
       stmatrix_x4_trans(smem_u32(h1 + swz(srow, schunk)), p1);
@@ -559,10 +588,23 @@ __device__ __forceinline__ void epilogue_tile_tr_heads(const EpiParams &ep, cons
 #pragma unroll
       for (int j2 = 0; j2 < 2; ++j2) {
         const size_t r0 = (size_t)tile * kBM + row_base + 8 * (2 * jj + j2) + 2 * (lane & 3);
+        if (ep.x32_natural_in) {
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          rx[j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
-          rx[j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+          for (int m = 0; m < 4; ++m) {
+            rx[j2][m][0] = ep.x32[r0 * kC + ch0 + 8 * m];
+            rx[j2][m][1] = ep.x32[(r0 + 1) * kC + ch0 + 8 * m];
+          }
+        } else {
+          const float4 v0 = *reinterpret_cast<const float4 *>(ep.x32 + r0 * kC + x32_slot(ch0));
+          const float4 v1 = *reinterpret_cast<const float4 *>(ep.x32 + (r0 + 1) * kC + x32_slot(ch0));
+          rx[j2][0][0] = v0.x;
+          rx[j2][1][0] = v0.y;
+          rx[j2][2][0] = v0.z;
+          rx[j2][3][0] = v0.w;
+          rx[j2][0][1] = v1.x;
+          rx[j2][1][1] = v1.y;
+          rx[j2][2][1] = v1.z;
+          rx[j2][3][1] = v1.w;
         }
       }
     }
@@ -1106,6 +1148,8 @@ __global__ void __launch_bounds__(kStemThreads, 3) stem_kernel(const float *obs,
         ph[j / 2] = F16Traits<T>::pack(hi[0], hi[1]);
         pl[j / 2] = F16Traits<T>::pack(lo[0], lo[1]);
       }
+      // x32 in the natural channel order: the first block's conv2 reads it
+      // so and writes the permuted order (x32_slot)
       float4 *xd = reinterpret_cast<float4 *>(x32 + r * kC + n0);
       xd[0] = make_float4(xv[0], xv[1], xv[2], xv[3]);
       xd[1] = make_float4(xv[4], xv[5], xv[6], xv[7]);
@@ -1449,6 +1493,7 @@ int scacchi_conv3x3(const void *input, const void *weights, const float *bias, i
   ep.head_out = head_out;
   ep.terms = 1;
   ep.x32 = nullptr;
+  ep.x32_natural_in = 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const uint64_t rows = scacchi_tower_rows(boards);
   return fp16 ? launch_conv<__half, false>(input, nullptr, weights, out0, out1, ep, rows, st)
@@ -1457,10 +1502,10 @@ int scacchi_conv3x3(const void *input, const void *weights, const float *bias, i
 
 int scacchi_conv3x3_split(const void *input, const void *input_lo, const void *weights, const float *bias,
                           int32_t mode, int32_t boards, int32_t fp16, int32_t terms, const float *bn_scale,
-                          const float *bn_shift, float *x32, const float *head_w, const float *head_b, void *out_hi,
-                          void *out_lo, float *head_out, void *stream) {
+                          const float *bn_shift, float *x32, int32_t x32_natural_in, const float *head_w,
+                          const float *head_b, void *out_hi, void *out_lo, float *head_out, void *stream) {
   if (!input || !input_lo || !weights || !bias || boards < 1 || mode < 0 || mode > 2 || (fp16 != 0 && fp16 != 1) ||
-      terms < 2 || terms > 3)
+      terms < 2 || terms > 3 || (x32_natural_in != 0 && x32_natural_in != 1))
     return SCACCHI_EINVAL;
   if (mode != kEpiConv1 && (!bn_scale || !bn_shift || !x32)) return SCACCHI_EINVAL;
   if (mode == kEpiHeads && (!head_w || !head_b || !head_out)) return SCACCHI_EINVAL;
@@ -1477,6 +1522,7 @@ int scacchi_conv3x3_split(const void *input, const void *input_lo, const void *w
   ep.bn_shift = bn_shift;
   ep.residual = nullptr;
   ep.x32 = x32;
+  ep.x32_natural_in = x32_natural_in;
   ep.head_w = head_w;
   ep.head_b = head_b;
   ep.head_out = head_out;
@@ -1551,11 +1597,13 @@ int scacchi_tower_forward(const scacchi_tower_weights *w, const float *obs, int3
     int rc;
     if (split) {
       rc = scacchi_conv3x3_split(a, a_lo, w1, w->conv_b + (2 * blk) * kC, kEpiConv1, boards, w->fp16, w->terms,
-                                 nullptr, nullptr, nullptr, nullptr, nullptr, h, h_lo, nullptr, stream);
+                                 nullptr, nullptr, nullptr, 0, nullptr, nullptr, h, h_lo, nullptr, stream);
       if (rc) return rc;
+      // the stem leaves x32 in the natural channel order; the first block's
+      // conv2 reads it so and writes the x32_slot order the others use
       rc = scacchi_conv3x3_split(h, h_lo, w2, w->conv_b + (2 * blk + 1) * kC, mode2, boards, w->fp16, w->terms, s2,
-                                 t2, x32, w->head_w, w->head_b, last ? nullptr : a, last ? nullptr : a_lo, feat,
-                                 stream);
+                                 t2, x32, blk == 0 ? 1 : 0, w->head_w, w->head_b, last ? nullptr : a,
+                                 last ? nullptr : a_lo, feat, stream);
     } else {
       rc = scacchi_conv3x3(a, w1, w->conv_b + (2 * blk) * kC, kEpiConv1, boards, w->fp16, nullptr, nullptr, nullptr,
                            nullptr, nullptr, h, nullptr, nullptr, stream);

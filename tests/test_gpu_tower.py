@@ -103,6 +103,22 @@ def test_single_conv_layer(cuda, mode, fp16):
     np.testing.assert_allclose(got, want, rtol=2e-2, atol=2e-2)
 
 
+# the fp32 residual stream keeps each row's channels permuted within their
+# 32-channel block: channel 32 q + 8 m + l (l < 8, m < 4) at 32 q + 4 l + m
+_C = np.arange(128)
+X32_SLOT = (_C & ~31) | ((_C & 7) << 2) | ((_C >> 3) & 3)
+
+
+def x32_stored(x: np.ndarray) -> np.ndarray:
+    out = np.empty_like(x)
+    out[..., X32_SLOT] = x
+    return out
+
+
+def x32_natural(y: np.ndarray) -> np.ndarray:
+    return y[..., X32_SLOT]
+
+
 def _split16(x: np.ndarray, fp16: bool):
     """x -> (hi, lo) 16-bit tensors with hi = round(x), lo = round(x - hi)."""
     hi = half(x, fp16)
@@ -110,13 +126,17 @@ def _split16(x: np.ndarray, fp16: bool):
     return hi, lo
 
 
+@pytest.mark.parametrize("natural_in", [0, 1], ids=["x32_permuted", "x32_natural_in"])
 @pytest.mark.parametrize("terms", [2, 3])
 @pytest.mark.parametrize("fp16", [False, True], ids=["bf16", "fp16"])
 @pytest.mark.parametrize("mode", [0, 1, 2], ids=["conv1", "conv2", "heads"])
-def test_single_conv_layer_split(cuda, mode, fp16, terms):
+def test_single_conv_layer_split(cuda, mode, fp16, terms, natural_in):
     """Split operands: the accumulator receives W_hi (A_hi + A_lo) (+ W_lo
     A_hi), the epilogue writes each 16-bit output as a hi / lo pair and keeps
-    the residual stream in fp32."""
+    the residual stream in fp32, read in the permuted channel order (or, for
+    the first block, the stem's natural order) and written permuted."""
+    if mode == 0 and natural_in:
+        pytest.skip("conv1 does not read the residual stream")
     from scacchi_b200 import _lib
 
     rng = np.random.default_rng(100 + mode + 3 * fp16 + 7 * terms)
@@ -137,7 +157,8 @@ def test_single_conv_layer_split(cuda, mode, fp16, terms):
     inp = half(to_padded(a_hi.float().numpy(), rows), fp16).to(dev)
     inp_lo = half(to_padded(a_lo.float().numpy(), rows), fp16).to(dev)
     wt = (torch.stack([w_hi, w_lo]) if terms == 3 else w_hi).contiguous().to(dev)
-    x32 = torch.from_numpy(to_padded(res, rows)).to(dev)
+    x32_in = to_padded(res, rows)
+    x32 = torch.from_numpy(x32_in if natural_in else x32_stored(x32_in)).to(dev)
     out_hi = torch.full((rows, 128), 7.0, dtype=dt, device=dev)
     out_lo = torch.full((rows, 128), 7.0, dtype=dt, device=dev)
     head = torch.zeros((rows, 8), dtype=torch.float32, device=dev)
@@ -145,7 +166,7 @@ def test_single_conv_layer_split(cuda, mode, fp16, terms):
     thw, thb = torch.from_numpy(hw).to(dev), torch.from_numpy(hb).to(dev)
     p = lambda t: C.c_void_p(t.data_ptr())
     rc = _lib.lib().scacchi_conv3x3_split(p(inp), p(inp_lo), p(wt), p(tb), mode, E, int(fp16), terms, p(tsc),
-                                          p(tsh), p(x32), p(thw), p(thb), p(out_hi), p(out_lo), p(head),
+                                          p(tsh), p(x32), natural_in, p(thw), p(thb), p(out_hi), p(out_lo), p(head),
                                           C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0
     torch.cuda.synchronize()
@@ -169,7 +190,7 @@ def test_single_conv_layer_split(cuda, mode, fp16, terms):
     a = np.maximum(x_new * sc + sh, 0)
     if mode == 1:
         # the residual stream is updated in place (the heads layer leaves it)
-        np.testing.assert_allclose(from_padded(x32.cpu().numpy(), E), x_new, rtol=1e-4, atol=1e-4)
+        np.testing.assert_allclose(from_padded(x32_natural(x32.cpu().numpy()), E), x_new, rtol=1e-4, atol=1e-4)
         np.testing.assert_allclose(from_padded(got_pair, E), a, rtol=1e-4, atol=1e-4)
         return
     want = np.maximum(a @ hw.T + hb, 0)
